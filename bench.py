@@ -1,0 +1,473 @@
+#!/usr/bin/env python
+"""Benchmark of the QVex hot path on B200: 4-bit g64 qmv over one decode step.
+
+Workload (the configuration the headline metric is quoted on): every
+4-bit group-64 linear of one decode step of a Qwen3.5-9B-shaped model (24 gated-DeltaNet
++ 8 gated-attention layers, hidden 4096, MLP 12288, vocab 248320; 145 projections,
+4.464 GB of packed weights), applied to x bf16 [M, K] ~ N(0,1) with M = 1.  Weights are
+synthetic (seeded): codes uniform 0..15, scales |N(0,1)|*0.002, biases -8*scale.  One
+"step" is the 145 qmv launches of one decode step, replayed from a CUDA graph (the
+launches carry programmatic-dependent-launch edges).  The weights total 4.46 GB, far
+above the 126 MB L2, so no flush is needed between steps.
+
+With --gpus N (torchrun, one rank per GPU) each projection is column-sharded: rank r
+owns a contiguous 1/N of the output rows (weights, scales, biases) and the shards are
+all-gathered over NCCL after each projection (strong scaling: total work fixed).
+
+Prints ONE JSON line (rank 0).  `--impl reference` times the reference's arithmetic on
+the host CPU cores instead (the oracle port of engine/kernels.py's qmv arithmetic: MLX,
+which the reference uses, is not installed here), on a bounded row sample of the same
+workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "qvex-3.5_b200"))
+
+METRIC = "4-bit qmv HBM GB/s (M=1) & %peak; decode tok/s Qwen3.5-9B-shape at 1/2/4/8 GPU"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=1, help="tokens per step (1 = batch-1 decode)")
+    ap.add_argument("--layers", type=int, default=32, help="decoder layers (32 = the full 9B shape)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the M=2/4/8 side measurements")
+    ap.add_argument("--profile", action="store_true",
+                    help="small run for profilers: no graph, no clocks, no CPU baseline")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ environment
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0, t1, gpu_indices):
+        sel = [p for (t, p) in self.samples if t0 - 0.15 <= t <= t1 + 0.15 and p[0] in gpu_indices]
+        if not sel:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(p[1]) for p in sel if num(p[1]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for p in sel:
+            for name, v in zip(names, p[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(sel[0][2]),
+                "reasons": sorted(reasons), "samples": len(sel)}
+
+
+# ------------------------------------------------------------------ workload
+
+def build_weights(torch, shape, rank, world, device, seed=0):
+    """Synthetic 4-bit g64 weights of one decode step, rows sharded over `world` ranks."""
+    from qvex.model import QLinear
+    lins = []
+    g = torch.Generator(device=device)
+    for i, (name, N, K) in enumerate(shape.decode_linears()):
+        if N % world:
+            raise ValueError(f"{name}: N={N} does not split over {world} ranks")
+        n = N // world
+        g.manual_seed(seed * 100003 + i)
+        # all 2^32 patterns equally likely => every 4-bit code uniform in 0..15
+        w = torch.randint(-2 ** 31, 2 ** 31, (N, K // 8), dtype=torch.int64, device=device, generator=g)
+        w = w.to(torch.int32)[rank * n:(rank + 1) * n].contiguous()
+        s = (torch.randn((N, K // 64), device=device, generator=g).abs() * 0.002).to(torch.bfloat16)
+        s = s[rank * n:(rank + 1) * n].contiguous()
+        b = (-8.0 * s.float()).to(torch.bfloat16)
+        lins.append((name, N, K, QLinear(w, s, b, 64, 4)))
+    return lins
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from qvex.shapes import Qwen35Shape, qlinear_bytes, qmv_bytes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    import qvex
+    qvex.load_library()
+
+    shape = Qwen35Shape(layers=args.layers)
+    M = args.m
+    lins = build_weights(torch, shape, rank, world, device)
+    Ks = sorted({K for _, _, K, _ in lins})
+    g = torch.Generator(device=device)
+    g.manual_seed(1234)
+    xs = {K: torch.randn((M, K), device=device, generator=g).to(torch.bfloat16) for K in Ks}
+    local_out = [torch.empty((M, l.out_features), dtype=torch.bfloat16, device=device) for _, _, _, l in lins]
+    full_out = [torch.empty((world, M, N // world), dtype=torch.bfloat16, device=device) for _, N, _, _ in lins]
+    launches_per_step = len(lins)
+
+    def step_qmv():
+        for (_, _, K, lin), out in zip(lins, local_out):
+            lin(xs[K], out=out)
+
+    def step_full():
+        for (_, _, K, lin), out, full in zip(lins, local_out, full_out):
+            lin(xs[K], out=out)
+            if world > 1:
+                dist.all_gather_into_tensor(full, out)
+
+    if args.profile:
+        for _ in range(max(args.warmup, 1)):
+            step_full()
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "launches_per_step": launches_per_step}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # warm the kernels (occupancy queries, module load) before capture
+    step_full()
+    torch.cuda.synchronize()
+    graph_full = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_full):
+        step_full()
+    graph_q = graph_full
+    if world > 1:
+        graph_q = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_q):
+            step_qmv()
+
+    def timed(graph, steps, warmup):
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.time()
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t1 = time.time()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            dist.barrier()
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, t0, t1
+
+    clocks = ClockSampler().start() if rank == 0 else None
+    ms_total, t0, t1 = timed(graph_full, args.steps, args.warmup)
+    if clocks:
+        clocks.stop()
+    ms_q, _, _ = timed(graph_q, args.steps, 3) if world > 1 else (ms_total, t0, t1)
+
+    bytes_full = sum(qmv_bytes(M, N, K) for _, N, K, _ in lins)           # whole job, per step
+    bytes_rank = sum(qmv_bytes(M, N // world, K) for _, N, K, _ in lins)  # this rank's kernels
+    weight_bytes = sum(qlinear_bytes(N, K) for _, N, K, _ in lins)
+    ms_step = ms_total / args.steps
+    value = bytes_full / (ms_step * 1e-3) / 1e9
+    achieved = bytes_rank / (ms_q / args.steps * 1e-3) / 1e9   # per-GPU qmv bytes / per-GPU qmv time
+    peak, peak_kind = peaks()
+
+    # side measurement: lm_head qmv alone (572 MB, one launch), events around each launch
+    lm = lins[-1][3]
+    lm_out = local_out[-1]
+    for _ in range(3):
+        lm(xs[4096], out=lm_out)
+    torch.cuda.synchronize()
+    reps = 20
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in ev:
+        a.record()
+        lm(xs[4096], out=lm_out)
+        b.record()
+    torch.cuda.synchronize()
+    lm_ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+    lm_gbs = qmv_bytes(M, lins[-1][1] // world, 4096) / (lm_ms * 1e-3) / 1e9
+
+    # e2e through the public API: host x -> device, the captured QLinear calls, logits -> host,
+    # synchronised every step (a decode loop needs the logits before the next token)
+    pin_x = {K: xs[K].cpu().pin_memory() for K in Ks}
+    logits_dev = full_out[-1] if world > 1 else local_out[-1]
+    pin_y = torch.empty(logits_dev.shape, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * 2 for t in pin_x.values())
+    d2h = pin_y.numel() * 2
+    e2e_steps = max(min(args.steps, 200), 10)
+    stream = torch.cuda.current_stream()
+    for i in range(e2e_steps + 3):
+        if i == 3:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            te0 = time.perf_counter()
+        for K in Ks:
+            xs[K].copy_(pin_x[K], non_blocking=True)
+        graph_full.replay()
+        pin_y.copy_(logits_dev, non_blocking=True)
+        stream.synchronize()
+    te1 = time.perf_counter()
+    e2e_s = te1 - te0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_val = bytes_full * e2e_steps / e2e_s / 1e9
+
+    extra = {}
+    if not args.no_extra and world == 1:
+        for m2 in (2, 4, 8):
+            xs2 = {K: torch.randn((m2, K), device=device, generator=g).to(torch.bfloat16) for K in Ks}
+            outs2 = [torch.empty((m2, l.out_features), dtype=torch.bfloat16, device=device) for _, _, _, l in lins]
+
+            def step_m():
+                for (_, _, K, lin), out in zip(lins, outs2):
+                    lin(xs2[K], out=out)
+            step_m()
+            torch.cuda.synchronize()
+            gm = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gm):
+                step_m()
+            ms_m, _, _ = timed(gm, max(args.steps // 4, 10), 3)
+            bm = sum(qmv_bytes(m2, N, K) for _, N, K, _ in lins)
+            extra[f"M={m2}"] = round(bm / (ms_m / max(args.steps // 4, 10) * 1e-3) / 1e9, 1)
+            del gm
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(torch, lins, xs, M, budget_s=3.0)
+
+    if rank == 0:
+        clk = clocks.summary(t0, t1, {str(local)}) if clocks else None
+        rec = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u4 codes, bf16 x/y, fp32 acc",
+            "data": "synthetic (seeded codes/scales/biases as config 0; x ~ N(0,1))",
+            "config": {"workload": "config 1: all 145 4-bit g64 linears of one Qwen3.5-9B-shaped decode step",
+                       "M": M, "layers": args.layers, "weight_bytes_per_step": weight_bytes,
+                       "parallelism": f"column-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (4.46 GB of weights per step)", "cuda_graph": True},
+            "tok_per_s": round(1000.0 / ms_step, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic_per_launch(bytes_rank / launches_per_step),
+                         "kernel": "qmv_kernel<1,32,4> (all launches of the step)"},
+            "lm_head_qmv": {"gbs": round(lm_gbs, 1), "ms": round(lm_ms, 4), "frac": round(lm_gbs / peak, 4)},
+            "qmv_gbs_by_m": extra,
+            "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "tok_per_s": round(e2e_steps / e2e_s, 1),
+                    "path": "pinned host x -> QLinear calls captured in a CUDA graph -> pinned host logits, sync/step"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        if cpu:
+            rec["cpu_baseline"] = cpu
+        print(json.dumps(rec))
+    del graph_full, graph_q
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def traffic_per_launch(algo_bytes_per_launch):
+    """DRAM bytes per launch from the committed ncu summary (ratio of measured DRAM bytes
+    to algorithmic bytes on the profiled case, applied to this launch size), or None."""
+    p = ROOT / "profiles" / "qmv_traffic_ratio.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_over_algorithmic:"):
+            return round(float(line.split(":", 1)[1]) * algo_bytes_per_launch)
+    return None
+
+
+# ------------------------------------------------------------------ CPU (reference arithmetic)
+
+def _cpu_sample(torch, lins, xs, M, row_frac):
+    """Host copies of the first `row_frac` of every linear's rows."""
+    import numpy as np
+    sample = []
+    for name, N, K, lin in lins:
+        n = max(8, int(lin.out_features * row_frac))
+        w = lin.w[:n].cpu().numpy().view(np.uint32)
+        s = lin.scales[:n].view(torch.int16).cpu().numpy().view(np.uint16)
+        b = lin.biases[:n].view(torch.int16).cpu().numpy().view(np.uint16)
+        x = xs[K][:M].view(torch.int16).cpu().numpy().view(np.uint16)
+        sample.append((x, w, s, b))
+    return sample
+
+
+def _time_cpu(sample, threads, budget_s, min_passes=1):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    from qvex.shapes import qmv_bytes
+    O.set_num_threads(threads)
+    byts = sum(qmv_bytes(x.shape[0], w.shape[0], x.shape[1]) for x, w, _, _ in sample)
+    for x, w, s, b in sample[:4]:  # warm
+        O.qmv_fast(x, w, s, b)
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        for x, w, s, b in sample:
+            O.qmv_fast(x, w, s, b)
+        passes += 1
+        el = time.perf_counter() - t0
+        if passes >= min_passes and el >= budget_s:
+            break
+    return byts * passes / el / 1e9, passes, el, byts
+
+
+def cpu_baseline(torch, lins, xs, M, budget_s):
+    threads = host_threads()
+    frac = 1 / 32
+    sample = _cpu_sample(torch, lins, xs, M, frac)
+    gbs, passes, el, byts = _time_cpu(sample, threads, budget_s)
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"first 1/32 of the rows of all 145 linears ({byts / 1e6:.0f} MB per pass), M={M}, "
+                      f"{passes} passes in {el:.1f} s; oracle/qvex_oracle.c orc_qmv_fast (the reference qmv "
+                      f"arithmetic, engine/kernels.py:146-174), OpenMP"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch  # only for seeded weight generation (CPU tensors)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle as O
+    from qvex.shapes import Qwen35Shape, qmv_bytes
+    shape = Qwen35Shape(layers=args.layers)
+    frac = 1 / 64
+    g = torch.Generator().manual_seed(0)
+    sample = []
+    for name, N, K in shape.decode_linears():
+        n = max(8, int(N * frac))
+        w = torch.randint(-2 ** 31, 2 ** 31, (n, K // 8), dtype=torch.int64, generator=g).to(torch.int32)
+        s = (torch.randn((n, K // 64), generator=g).abs() * 0.002).to(torch.bfloat16)
+        b = (-8.0 * s.float()).to(torch.bfloat16)
+        x = torch.randn((args.m, K), generator=g).to(torch.bfloat16)
+        sample.append((x.view(torch.int16).numpy().view(np.uint16), w.numpy().view(np.uint32),
+                       s.view(torch.int16).numpy().view(np.uint16), b.view(torch.int16).numpy().view(np.uint16)))
+    threads = host_threads()
+    O.set_num_threads(threads)
+    byts = sum(qmv_bytes(x.shape[0], w.shape[0], x.shape[1]) for x, w, _, _ in sample)
+
+    def one_pass():
+        for x, w, s, b in sample:
+            O.qmv_fast(x, w, s, b)
+    for _ in range(args.warmup):
+        one_pass()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_pass()
+    el = time.perf_counter() - t0
+    value = byts * args.steps / el / 1e9
+    rec = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes, bf16 x/y, fp32 acc",
+        "data": "synthetic (seeded codes/scales/biases as config 0; x ~ N(0,1))",
+        "config": {"workload": "config 1: all 145 4-bit g64 linears of one Qwen3.5-9B-shaped decode step",
+                   "M": args.m, "layers": args.layers, "sample": "first 1/64 of the rows of every linear"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"first 1/64 of the rows of all 145 linears ({byts / 1e6:.0f} MB per step); "
+                                   "MLX (the reference's engine) is not installed, so the reference qmv arithmetic "
+                                   "(engine/kernels.py:146-174) runs as the C oracle port orc_qmv_fast, OpenMP"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(rec))
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,134 @@
+/*
+ * qvex.h -- C ABI of libqvex, the B200 (sm_100a) implementation of QVex's quantized
+ * linear + gated-DeltaNet hot path.
+ *
+ * Conventions for every entry point:
+ *   - returns an int status (QVX_OK = 0; see the enum below); the message of the last
+ *     failure on the calling thread is available from qvx_last_error();
+ *   - all tensors are caller-owned DEVICE buffers, dense and row-major (C order);
+ *     bf16 tensors are passed as `void*` holding IEEE bfloat16 bit patterns;
+ *   - work is enqueued on the caller's stream (`void* stream` is a cudaStream_t;
+ *     NULL means the legacy default stream) and the call returns without
+ *     synchronising; inputs are never written;
+ *   - no entry point allocates device memory; the ones that need scratch space take a
+ *     caller-provided workspace and report its size through a *_workspace_size call;
+ *   - calls on distinct streams with distinct output/workspace buffers may run
+ *     concurrently from different host threads.
+ *
+ * Quantized weight format (MLX affine, bits = 4, group_size = 64), for a weight of
+ * N output rows and K inputs:
+ *   w       uint32 [N, K/8]   element k of row n is (w[n, k/8] >> 4*(k%8)) & 0xF
+ *   scales  bf16   [N, K/64]
+ *   biases  bf16   [N, K/64]  weight[n,k] = scales[n,k/64] * q[n,k] + biases[n,k/64]
+ */
+#ifndef QVEX_H_
+#define QVEX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum qvx_status {
+  QVX_OK = 0,
+  QVX_ERR_INVALID = 1,      /* bad shape, null pointer or inconsistent sizes */
+  QVX_ERR_UNSUPPORTED = 2,  /* valid for MLX but not implemented here (bits, group size) */
+  QVX_ERR_ALIGN = 3,        /* a pointer is not aligned as the kernel requires */
+  QVX_ERR_CUDA = 4,         /* a CUDA runtime/driver call failed */
+  QVX_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up (see qvx_device_status) */
+  QVX_ERR_WORKSPACE = 6     /* workspace missing or smaller than *_workspace_size() */
+};
+
+/* Library version as 10000*major + 100*minor + patch. */
+int qvx_version(void);
+
+/* Human-readable text of the last failure on the calling thread ("" if none). */
+const char* qvx_last_error(void);
+
+/* Reads (and clears) the device-side status word that bounded waits in the kernels
+ * set when they give up; returns QVX_OK or QVX_ERR_TIMEOUT in *device_status.
+ * Synchronises `stream`. */
+int qvx_device_status(void* stream, int* device_status);
+
+/* ---------------------------------------------------------------- quantized matmul */
+
+/* y[M,N] (bf16) = x[M,K] (bf16) @ dequant(w)^T, for 1 <= M <= 8 (decode / verify).
+ * Replaces mx.quantized_matmul(x, w, scales, biases, transpose=True, group_size=64,
+ * bits=4) as called by QLinear.__call__ (engine/model.py:87-91) at M = 1 and 2, and
+ * the reference's own multi-row kernel qmv_multi (engine/kernels.py:197-211).
+ * SIMT kernel, fp32 accumulation.  Requires K % 64 == 0 and K <= 32768;
+ * x must be 16-byte aligned, w 16-byte aligned. */
+int qvx_qmv(const void* x, const uint32_t* w, const void* scales, const void* biases,
+            void* y, int M, int N, int K, int group_size, int bits, void* stream);
+
+/* Bytes of workspace qvx_qmm needs for these sizes. */
+size_t qvx_qmm_workspace_size(int M, int N, int K);
+
+/* y[M,N] (bf16) = x[M,K] (bf16) @ dequant(w)^T for any M >= 1 (prefill; built for
+ * M >= 16).  Replaces mx.quantized_matmul(...) at M = 512 prefill chunks
+ * (engine/engine.py:25,239 -> engine/model.py:87-91).  tcgen05 tensor-core kernel:
+ * weights are dequantised to fp16 in tensor memory, x is converted to fp16 with an
+ * exact per-row power-of-two scale, fp32 accumulation.  Requires K % 64 == 0 and a
+ * workspace of qvx_qmm_workspace_size(M, N, K) bytes (256-byte aligned). */
+int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
+            void* y, int M, int N, int K, int group_size, int bits, void* workspace,
+            size_t workspace_bytes, void* stream);
+
+/* Dispatcher with mx.quantized_matmul's semantics: qvx_qmv for M <= 8, qvx_qmm above.
+ * The workspace may be NULL when M <= 8. */
+int qvx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
+                         const void* biases, void* y, int M, int N, int K, int group_size,
+                         int bits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- quantize / dequantize */
+
+enum qvx_quant_variant {
+  QVX_QUANT_MINMAX = 0,     /* scale = (max-min)/15, bias = min (per group) */
+  QVX_QUANT_ZERO_EXACT = 1  /* larger-magnitude edge is the bias, 0.0 exactly representable */
+};
+
+/* w bf16 [N,K] -> wq uint32 [N,K/8], scales/biases bf16 [N,K/64].  Replaces
+ * mx.quantize(w, group_size=64, bits=4) (tools/fetch_mtp.py:99,
+ * bench/qmv_kernel_bench.py:14) with the packing of quant/quantize.py:71-75.
+ * Codes are rint((w - bias) / scale) clipped to 0..15 in IEEE fp32, bit-exact with
+ * the CPU restatement. */
+int qvx_quantize(const void* w, uint32_t* wq, void* scales, void* biases, int N, int K,
+                 int group_size, int bits, int variant, void* stream);
+
+/* wq/scales/biases -> out bf16 [N,K], out = bf16(fma(scale, q, bias)).  Replaces
+ * mx.dequantize (engine/model.py:127, quant/quantize.py:101). */
+int qvx_dequantize(const uint32_t* wq, const void* scales, const void* biases, void* out,
+                   int N, int K, int group_size, int bits, void* stream);
+
+/* Row gather + dequantize: out[i,:] = dequant(row ids[i]) for i < n_ids, ids int32.
+ * Replaces QEmbedding.__call__ (engine/model.py:126-130).  Ids outside [0, N) produce
+ * QVX_ERR_INVALID through the device status word and zero rows. */
+int qvx_dequantize_rows(const uint32_t* wq, const void* scales, const void* biases,
+                        const int32_t* ids, int n_ids, void* out, int N, int K,
+                        int group_size, int bits, void* stream);
+
+/* ---------------------------------------------------------------- gated DeltaNet */
+
+/* Replaces gated_delta(q, k, v, a, b, A_log, dt_bias, state, keep_mid)
+ * (engine/kernels.py:92-116).
+ *   q, k      bf16 [B, T, Hk, Dk]      v  bf16 [B, T, Hv, Dv]
+ *   a, b      bf16 [B, T, Hv]          A_log, dt_bias fp32 [Hv]
+ *   state_in  fp32 [B, Hv, Dv, Dk]     y  bf16 [B, T, Hv, Dv]
+ *   state_out fp32 [B, Hv, Dv, Dk]     state_mid fp32 [B, Hv, Dv, Dk] or NULL
+ * Per step: g = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b);
+ * s <- g*s; kv = s.k; delta = (v - kv)*beta; s <- s + k*delta; y = s.q.
+ * state_mid (if non-NULL) receives the state before the last step (rollback).
+ * Requires Hv % Hk == 0, Dk == 128 or 64 or 32, Dv % 16 == 0, T >= 1.
+ * state_out may alias state_in (in-place update); y must not alias inputs. */
+int qvx_gated_delta(const void* q, const void* k, const void* v, const void* a, const void* b,
+                    const float* A_log, const float* dt_bias, const float* state_in, void* y,
+                    float* state_out, float* state_mid, int B, int T, int Hk, int Hv, int Dk,
+                    int Dv, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QVEX_H_ */

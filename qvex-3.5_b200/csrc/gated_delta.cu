@@ -1,0 +1,211 @@
+// Gated-DeltaNet recurrence with in-kernel gates and optional pre-last-step snapshot.
+//
+// Replaces gated_delta(q, k, v, a, b, A_log, dt_bias, state, keep_mid)
+// (engine/kernels.py:92-116, Metal source :11-75).  Per (batch b, value head hv,
+// value row dv) the fp32 state row s[Dk] follows, for t = 0..T-1:
+//   g = exp(-exp(A_log) * softplus(a + dt_bias))   softplus(x) = x for x > 20
+//   beta = sigmoid(b)
+//   s <- g s;  kv = s.k;  delta = (v - kv) beta;  s <- s + k delta;  y = s.q
+// with key head hk = hv / (Hv / Hk) (grouped heads).
+//
+// Layout.  A warp owns RW = 4 value rows of one head; lane l holds state elements
+// [l*Dk/32, (l+1)*Dk/32) of each of its rows in registers (the reference's lane
+// ownership), so the state never leaves the SM between steps and HBM sees it once in and
+// once out (plus once for the snapshot).  A CTA is 4 warps = 16 rows of one head.
+// Per step the four row dot products are reduced together with a transposing butterfly
+// (6 shuffles for 4 values instead of 20), then broadcast.  The next step's q/k/v/a/b
+// are loaded before the current step is computed, so their latency hides behind the
+// reductions.
+#include "common.cuh"
+
+namespace qvx {
+
+constexpr int kGdRowsPerWarp = 4;
+constexpr int kGdWarps = 4;
+
+// 4 values -> lane l holds the total of value (l >> 3); then broadcast all four.
+__device__ __forceinline__ void reduce4_all(float (&p)[4], int lane) {
+  {
+    const bool up = lane & 16;
+    const float s0 = up ? p[0] : p[2], s1 = up ? p[1] : p[3];
+    const float k0 = up ? p[2] : p[0], k1 = up ? p[3] : p[1];
+    p[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 16);
+    p[1] = k1 + __shfl_xor_sync(0xffffffffu, s1, 16);
+  }
+  {
+    const bool up = lane & 8;
+    const float s0 = up ? p[0] : p[1];
+    const float k0 = up ? p[1] : p[0];
+    p[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 8);
+  }
+  p[0] += __shfl_xor_sync(0xffffffffu, p[0], 4);
+  p[0] += __shfl_xor_sync(0xffffffffu, p[0], 2);
+  p[0] += __shfl_xor_sync(0xffffffffu, p[0], 1);
+  const float t = p[0];
+  p[0] = __shfl_sync(0xffffffffu, t, 0);
+  p[1] = __shfl_sync(0xffffffffu, t, 8);
+  p[2] = __shfl_sync(0xffffffffu, t, 16);
+  p[3] = __shfl_sync(0xffffffffu, t, 24);
+}
+
+template <int NPT>
+__device__ __forceinline__ void load_bf16_vec(const __nv_bfloat16* p, float (&out)[NPT]) {
+  if constexpr (NPT == 4) {
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    out[0] = __uint_as_float(t.x << 16); out[1] = __uint_as_float(t.x & 0xffff0000u);
+    out[2] = __uint_as_float(t.y << 16); out[3] = __uint_as_float(t.y & 0xffff0000u);
+  } else if constexpr (NPT == 2) {
+    const uint32_t t = *reinterpret_cast<const uint32_t*>(p);
+    out[0] = __uint_as_float(t << 16); out[1] = __uint_as_float(t & 0xffff0000u);
+  } else {
+    out[0] = __bfloat162float(*p);
+  }
+}
+
+struct GdStep {
+  float q[4], k[4], v[kGdRowsPerWarp], a, b;
+};
+
+template <int NPT>
+__device__ __forceinline__ void gd_load_step(GdStep& s, const __nv_bfloat16* qp, const __nv_bfloat16* kp,
+                                             const __nv_bfloat16* vp, const __nv_bfloat16* ap,
+                                             const __nv_bfloat16* bp) {
+  float tq[NPT], tk[NPT];
+  load_bf16_vec<NPT>(qp, tq);
+  load_bf16_vec<NPT>(kp, tk);
+#pragma unroll
+  for (int i = 0; i < NPT; ++i) { s.q[i] = tq[i]; s.k[i] = tk[i]; }
+  const uint2 tv = *reinterpret_cast<const uint2*>(vp);  // 4 consecutive bf16 rows
+  s.v[0] = __uint_as_float(tv.x << 16); s.v[1] = __uint_as_float(tv.x & 0xffff0000u);
+  s.v[2] = __uint_as_float(tv.y << 16); s.v[3] = __uint_as_float(tv.y & 0xffff0000u);
+  s.a = __bfloat162float(*ap);
+  s.b = __bfloat162float(*bp);
+}
+
+template <int NPT>
+__global__ void __launch_bounds__(kGdWarps * 32) gated_delta_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+    const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, const float* __restrict__ A_log,
+    const float* __restrict__ dt_bias, const float* state_in, __nv_bfloat16* __restrict__ y, float* state_out,
+    float* __restrict__ state_mid, int T, int Hk, int Hv, int Dv) {
+  constexpr int Dk = NPT * 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = blockIdx.y;  // b * Hv + hv
+  const int bi = n / Hv, hv = n % Hv, hk = hv / (Hv / Hk);
+  const int dv0 = (blockIdx.x * kGdWarps + warp) * kGdRowsPerWarp;
+  if (dv0 >= Dv) return;  // Dv % 16 == 0 is checked on the host, so whole warps exit
+
+  const float A = expf(A_log[hv]);
+  const float dt = dt_bias[hv];
+
+  float st[kGdRowsPerWarp][NPT];
+#pragma unroll
+  for (int r = 0; r < kGdRowsPerWarp; ++r) {
+    const float* src = state_in + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT;
+#pragma unroll
+    for (int i = 0; i < NPT; ++i) st[r][i] = src[i];
+  }
+
+  const size_t qk_step = (size_t)Hk * Dk, v_step = (size_t)Hv * Dv, ab_step = Hv;
+  const __nv_bfloat16* qp = q + ((size_t)bi * T * Hk + hk) * Dk + lane * NPT;
+  const __nv_bfloat16* kp = k + ((size_t)bi * T * Hk + hk) * Dk + lane * NPT;
+  const __nv_bfloat16* vp = v + ((size_t)bi * T * Hv + hv) * Dv + dv0;
+  const __nv_bfloat16* ap = a + (size_t)bi * T * Hv + hv;
+  const __nv_bfloat16* bp = b + (size_t)bi * T * Hv + hv;
+  __nv_bfloat16* yp = y + ((size_t)bi * T * Hv + hv) * Dv + dv0;
+
+  GdStep cur, nxt;
+  gd_load_step<NPT>(cur, qp, kp, vp, ap, bp);
+  for (int t = 0; t < T; ++t) {
+    if (t + 1 < T)
+      gd_load_step<NPT>(nxt, qp + (t + 1) * qk_step, kp + (t + 1) * qk_step, vp + (t + 1) * v_step,
+                        ap + (t + 1) * ab_step, bp + (t + 1) * ab_step);
+    if (state_mid != nullptr && t == T - 1) {
+#pragma unroll
+      for (int r = 0; r < kGdRowsPerWarp; ++r) {
+        float* dst = state_mid + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT;
+#pragma unroll
+        for (int i = 0; i < NPT; ++i) dst[i] = st[r][i];
+      }
+    }
+    const float xa = cur.a + dt;
+    const float sp = xa > 20.0f ? xa : logf(1.0f + expf(xa));
+    const float g = expf(-A * sp);
+    const float beta = 1.0f / (1.0f + expf(-cur.b));
+
+    float p[4];
+#pragma unroll
+    for (int r = 0; r < kGdRowsPerWarp; ++r) {
+      float kv = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NPT; ++i) {
+        st[r][i] *= g;
+        kv = fmaf(st[r][i], cur.k[i], kv);
+      }
+      p[r] = kv;
+    }
+    reduce4_all(p, lane);
+#pragma unroll
+    for (int r = 0; r < kGdRowsPerWarp; ++r) {
+      const float delta = (cur.v[r] - p[r]) * beta;
+      float o = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NPT; ++i) {
+        st[r][i] = fmaf(cur.k[i], delta, st[r][i]);
+        o = fmaf(st[r][i], cur.q[i], o);
+      }
+      p[r] = o;
+    }
+    reduce4_all(p, lane);
+    if (lane < kGdRowsPerWarp) {
+      const float o = lane == 0 ? p[0] : lane == 1 ? p[1] : lane == 2 ? p[2] : p[3];
+      yp[(size_t)t * v_step + lane] = __float2bfloat16_rn(o);
+    }
+    cur = nxt;
+  }
+
+#pragma unroll
+  for (int r = 0; r < kGdRowsPerWarp; ++r) {
+    float* dst = state_out + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT;
+#pragma unroll
+    for (int i = 0; i < NPT; ++i) dst[i] = st[r][i];
+  }
+}
+
+}  // namespace qvx
+
+extern "C" int qvx_gated_delta(const void* q, const void* k, const void* v, const void* a, const void* b,
+                               const float* A_log, const float* dt_bias, const float* state_in, void* y,
+                               float* state_out, float* state_mid, int B, int T, int Hk, int Hv, int Dk, int Dv,
+                               void* stream) {
+  using namespace qvx;
+  if (B < 1 || T < 1 || Hk < 1 || Hv < 1 || Hv % Hk != 0 || Dv < 16 || Dv % 16 != 0)
+    return fail(QVX_ERR_INVALID, "qvx_gated_delta: bad shape B=%d T=%d Hk=%d Hv=%d Dk=%d Dv=%d", B, T, Hk, Hv, Dk,
+                Dv);
+  if (Dk != 32 && Dk != 64 && Dk != 128)
+    return fail(QVX_ERR_UNSUPPORTED, "qvx_gated_delta: Dk=%d (32, 64 or 128 supported)", Dk);
+  if (!q || !k || !v || !a || !b || !A_log || !dt_bias || !state_in || !y || !state_out)
+    return fail(QVX_ERR_INVALID, "qvx_gated_delta: null pointer");
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(v, 8) || !aligned(state_in, 16) || !aligned(state_out, 16) ||
+      (state_mid && !aligned(state_mid, 16)))
+    return fail(QVX_ERR_ALIGN, "qvx_gated_delta: q/k/v need 8-byte and states 16-byte alignment");
+  const dim3 grid(Dv / (kGdRowsPerWarp * kGdWarps) + (Dv % (kGdRowsPerWarp * kGdWarps) ? 1 : 0), B * Hv, 1);
+  const dim3 block(kGdWarps * 32, 1, 1);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto qq = static_cast<const __nv_bfloat16*>(q);
+  auto kk = static_cast<const __nv_bfloat16*>(k);
+  auto vv = static_cast<const __nv_bfloat16*>(v);
+  auto aa = static_cast<const __nv_bfloat16*>(a);
+  auto bb = static_cast<const __nv_bfloat16*>(b);
+  auto yy = static_cast<__nv_bfloat16*>(y);
+  if (Dk == 128)
+    gated_delta_kernel<4><<<grid, block, 0, s>>>(qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
+                                                 state_mid, T, Hk, Hv, Dv);
+  else if (Dk == 64)
+    gated_delta_kernel<2><<<grid, block, 0, s>>>(qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
+                                                 state_mid, T, Hk, Hv, Dv);
+  else
+    gated_delta_kernel<1><<<grid, block, 0, s>>>(qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
+                                                 state_mid, T, Hk, Hv, Dv);
+  return check_launch("qvx_gated_delta");
+}

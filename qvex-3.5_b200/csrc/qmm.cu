@@ -1,0 +1,134 @@
+// Prefill quantized matmul entry points (M >= 9): workspace sizing, the x -> fp16
+// prepass, and the dispatcher with mx.quantized_matmul semantics.
+//
+// The tensor-core main loop lives in qmm_tc.cu.  Precision design: tcgen05 kind::f16
+// needs both operands of one type.  Dequantised weights rounded to bf16 carry ~1e-3
+// relative error per weight, which alone puts the bf16 output at rel-L2 ~2.5e-3 of the
+// exact result; fp16 (11 significant bits) brings it to ~3e-4.  So both operands are
+// fp16: the weights are dequantised to fp16 inside the kernel, and x is converted here,
+// row m scaled by an exact power of two 2^-e[m] that puts max|x[m,:]| in [2^14, 2^15)
+// (no overflow, full fp16 precision); the epilogue multiplies by 2^e[m].
+//
+// Workspace layout (256-byte aligned sections):
+//   [0]            x16   fp16  [M, K]
+//   [off_exp]      e     int32 [M]
+#include "common.cuh"
+
+namespace qvx {
+
+int qmm_tc_launch(const __half* x16, const int32_t* xexp, const uint32_t* w, const uint16_t* sc,
+                  const uint16_t* bi, __nv_bfloat16* y, int M, int N, int K, cudaStream_t stream);
+int qmv_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
+                int K, cudaStream_t stream);
+int check_qparams(const char* who, const void* x, const uint32_t* w, const void* s, const void* b, const void* y,
+                  int M, int N, int K, int group_size, int bits);
+
+static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct QmmWorkspace {
+  size_t off_x16, off_exp, total;
+};
+
+static QmmWorkspace qmm_ws_layout(int M, int K) {
+  QmmWorkspace l;
+  l.off_x16 = 0;
+  l.off_exp = align256((size_t)M * K * sizeof(__half));
+  l.total = l.off_exp + align256((size_t)M * sizeof(int32_t));
+  return l;
+}
+
+// One CTA per row of x: max|x| -> exponent e (2^-e scaling), then the scaled fp16 copy.
+__global__ void __launch_bounds__(256) x_to_f16_kernel(const __nv_bfloat16* __restrict__ x, __half* __restrict__ x16,
+                                                      int32_t* __restrict__ xexp, int K) {
+  __shared__ float red[8];
+  const int m = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)m * K);
+  const int n16 = K / 8;  // 16-byte chunks (K % 64 == 0)
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+    const uint4 t = xr[i];
+    const uint32_t u[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h)
+      mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(u[h] << 16)), fabsf(__uint_as_float(u[h] & 0xffff0000u))));
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  mx = red[0];
+  // e such that mx * 2^-e lies in [2^14, 2^15); an all-zero or non-finite row keeps e = 0
+  int e = 0;
+  if (mx > 0.0f && isfinite(mx)) {
+    int ex;
+    frexpf(mx, &ex);         // mx = f * 2^ex, f in [0.5, 1)
+    e = max(ex - 15, -126);  // keeps 2^-e a finite float
+  }
+  const float scale = ldexpf(1.0f, -e);
+  uint2* outr = reinterpret_cast<uint2*>(x16 + (size_t)m * K);
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+    const uint4 t = xr[i];
+    const uint32_t u[4] = {t.x, t.y, t.z, t.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const __half2 p = __floats2half2_rn(__uint_as_float(u[h] << 16) * scale,
+                                          __uint_as_float(u[h] & 0xffff0000u) * scale);
+      o[h] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    outr[2 * i] = make_uint2(o[0], o[1]);
+    outr[2 * i + 1] = make_uint2(o[2], o[3]);
+  }
+  if (threadIdx.x == 0) xexp[m] = e;
+}
+
+int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
+                int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const QmmWorkspace l = qmm_ws_layout(M, K);
+  if (!workspace || workspace_bytes < l.total)
+    return fail(QVX_ERR_WORKSPACE, "qvx_qmm: workspace of %zu bytes needed, %zu given", l.total,
+                workspace ? workspace_bytes : (size_t)0);
+  if (!aligned(workspace, 256)) return fail(QVX_ERR_ALIGN, "qvx_qmm: workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  __half* x16 = reinterpret_cast<__half*>(ws + l.off_x16);
+  int32_t* xexp = reinterpret_cast<int32_t*>(ws + l.off_exp);
+  x_to_f16_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), x16, xexp, K);
+  int rc = check_launch("qvx_qmm prepass");
+  if (rc) return rc;
+  return qmm_tc_launch(x16, xexp, w, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
+                       static_cast<__nv_bfloat16*>(y), M, N, K, stream);
+}
+
+}  // namespace qvx
+
+extern "C" size_t qvx_qmm_workspace_size(int M, int N, int K) {
+  (void)N;
+  if (M < 1 || K < 1) return 0;
+  return qvx::qmm_ws_layout(M, K).total;
+}
+
+extern "C" int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M,
+                       int N, int K, int group_size, int bits, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  int rc = qvx::check_qparams("qvx_qmm", x, w, scales, biases, y, M, N, K, group_size, bits);
+  if (rc) return rc;
+  return qvx::qmm_checked(x, w, scales, biases, y, M, N, K, workspace, workspace_bytes,
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qvx_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                                    void* y, int M, int N, int K, int group_size, int bits, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  int rc = qvx::check_qparams("qvx_quantized_matmul", x, w, scales, biases, y, M, N, K, group_size, bits);
+  if (rc) return rc;
+  if (M <= 8) return qvx::qmv_checked(x, w, scales, biases, y, M, N, K, static_cast<cudaStream_t>(stream));
+  return qvx::qmm_checked(x, w, scales, biases, y, M, N, K, workspace, workspace_bytes,
+                          static_cast<cudaStream_t>(stream));
+}

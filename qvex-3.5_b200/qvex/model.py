@@ -1,0 +1,73 @@
+"""The reference's hot-path building blocks (engine/model.py) on libqvex.
+
+``QLinear`` (engine/model.py:80-104), ``QEmbedding`` (:121-130) and ``RecurrentCache``
+(:179-193) keep their constructor arguments, attributes and methods, so code written
+against the reference's classes runs unchanged with torch CUDA tensors.
+"""
+from __future__ import annotations
+
+import torch
+
+from .core import dequantize_rows, quantized_matmul
+
+
+class QLinear:
+    """Affine-quantized linear layer (y = x @ W^T)."""
+
+    def __init__(self, w, scales, biases, group_size=64, bits=4):
+        self.w, self.scales, self.biases = w, scales, biases
+        self.group_size, self.bits = group_size, bits
+
+    @property
+    def out_features(self) -> int:
+        return self.w.shape[0]
+
+    @property
+    def in_features(self) -> int:
+        return self.w.shape[1] * 32 // self.bits
+
+    def __call__(self, x, *, out=None, workspace=None):
+        return quantized_matmul(x, self.w, self.scales, self.biases, transpose=True,
+                                group_size=self.group_size, bits=self.bits, out=out, workspace=workspace)
+
+    @staticmethod
+    def fuse(layers: list["QLinear"]) -> "QLinear":
+        """Stack output rows of several layers sharing the same input (lossless)."""
+        l0 = layers[0]
+        if not all((l.group_size, l.bits) == (l0.group_size, l0.bits) for l in layers):
+            raise AssertionError("fused layers must share the quantization (bits, group size)")
+        return QLinear(
+            torch.cat([l.w for l in layers]),
+            torch.cat([l.scales for l in layers]),
+            torch.cat([l.biases for l in layers]),
+            l0.group_size, l0.bits,
+        )
+
+
+class QEmbedding:
+    def __init__(self, w, scales, biases, group_size=64, bits=4):
+        self.w, self.scales, self.biases = w, scales, biases
+        self.group_size, self.bits = group_size, bits
+
+    def __call__(self, ids):
+        return dequantize_rows(self.w, self.scales, self.biases, ids, group_size=self.group_size, bits=self.bits)
+
+
+class RecurrentCache:
+    """Conv + SSM state of one gated-DeltaNet layer, with one-token rollback."""
+
+    def __init__(self):
+        self.conv = None   # [B, K-1, conv_dim]
+        self.ssm = None    # [B, Hv, Dv, Dk] float32
+        self.offset = 0
+        self.conv_prev = self.ssm_prev = None  # state one token back (speculative decoding)
+
+    def state(self):
+        return [x for x in (self.conv, self.ssm) if x is not None]
+
+    def rollback(self, n=1):
+        if not (n == 1 and self.ssm_prev is not None):
+            raise AssertionError("can only roll back the last token")
+        self.conv, self.ssm = self.conv_prev, self.ssm_prev
+        self.conv_prev = self.ssm_prev = None
+        self.offset -= 1

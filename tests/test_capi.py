@@ -1,0 +1,116 @@
+"""libqvex.so: it builds, loads, exports every entry point of include/qvex.h, and rejects
+bad arguments before touching a GPU.  CPU only (no compute calls)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "qvex.h"
+
+
+def header_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(qvx_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    from qvex import _lib
+    from qvex.build import build
+    build()
+    return _lib.lib()
+
+
+def test_every_header_symbol_is_exported(L):
+    names = header_functions()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(L, n), n
+
+
+def test_binding_table_covers_header():
+    from qvex import _lib
+    assert sorted(_lib.SIGNATURES) == header_functions()
+
+
+def test_version(L):
+    assert L.qvx_version() >= 100
+
+
+P = ctypes.c_void_p
+DUMMY = P(4096)  # an aligned non-null address: never dereferenced, validation fails first
+
+
+@pytest.mark.parametrize("M,N,K,gs,bits,code", [
+    (0, 8, 64, 64, 4, 1),      # M < 1
+    (9, 8, 64, 64, 4, 1),      # qmv is M <= 8
+    (1, 8, 100, 64, 4, 1),     # K % 64
+    (1, 0, 64, 64, 4, 1),      # N < 1
+    (1, 8, 64, 32, 4, 2),      # group size not implemented
+    (1, 8, 64, 64, 3, 2),      # 3-bit not implemented
+])
+def test_qmv_rejects_bad_arguments(L, M, N, K, gs, bits, code):
+    rc = L.qvx_qmv(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, M, N, K, gs, bits, None)
+    assert rc == code
+    assert L.qvx_last_error()
+
+
+def test_qmv_rejects_misaligned_x(L):
+    assert L.qvx_qmv(P(4098), DUMMY, DUMMY, DUMMY, DUMMY, 1, 8, 64, 64, 4, None) == 3
+
+
+def test_qmm_workspace_checks(L):
+    need = L.qvx_qmm_workspace_size(64, 128, 256)
+    assert need >= 64 * 256 * 2
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, None, 0, None) == 6
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, DUMMY, need - 1, None) == 6
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, P(4096 + 16), need, None) == 3
+
+
+def test_gated_delta_rejects_bad_shapes(L):
+    args = [DUMMY] * 11
+    assert L.qvx_gated_delta(*args, 1, 1, 3, 32, 128, 128, None) == 1    # Hv % Hk
+    assert L.qvx_gated_delta(*args, 1, 1, 16, 32, 96, 128, None) == 2    # Dk not 32/64/128
+    assert L.qvx_gated_delta(*args, 1, 0, 16, 32, 128, 128, None) == 1   # T < 1
+    assert L.qvx_gated_delta(*args, 1, 1, 16, 32, 128, 120, None) == 1   # Dv % 16
+
+
+def test_quantize_rejects(L):
+    assert L.qvx_quantize(DUMMY, DUMMY, DUMMY, DUMMY, 4, 100, 64, 4, 0, None) == 1
+    assert L.qvx_quantize(DUMMY, DUMMY, DUMMY, DUMMY, 4, 128, 64, 4, 7, None) == 1
+    assert L.qvx_quantize(DUMMY, DUMMY, DUMMY, DUMMY, 4, 128, 128, 4, 0, None) == 2
+
+
+def test_python_front_end_rejects_cpu_tensors():
+    import torch
+    import qvex
+    x = torch.zeros(1, 64, dtype=torch.bfloat16)
+    w = torch.zeros(8, 8, dtype=torch.int32)
+    s = torch.zeros(8, 1, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        qvex.quantized_matmul(x, w, s, s)
+    with pytest.raises(NotImplementedError):
+        qvex.quantized_matmul(x, w, s, s, bits=3)
+    with pytest.raises(NotImplementedError):
+        qvex.quantized_matmul(x, w, s, s, transpose=False)
+
+
+def test_qlinear_fuse_and_rollback_host_logic():
+    import torch
+    from qvex import QLinear, RecurrentCache
+    a = QLinear(torch.zeros(4, 8, dtype=torch.int32), torch.zeros(4, 1), torch.ones(4, 1), 64, 4)
+    b = QLinear(torch.ones(2, 8, dtype=torch.int32), torch.ones(2, 1), torch.zeros(2, 1), 64, 4)
+    f = QLinear.fuse([a, b])
+    assert f.w.shape == (6, 8) and f.out_features == 6 and f.in_features == 64
+    assert torch.equal(f.w[4:], b.w)
+    with pytest.raises(AssertionError):
+        QLinear.fuse([a, QLinear(b.w, b.scales, b.biases, 32, 4)])
+    c = RecurrentCache()
+    with pytest.raises(AssertionError):
+        c.rollback(1)
+    c.ssm, c.conv, c.offset = "s1", "c1", 5
+    c.ssm_prev, c.conv_prev = "s0", "c0"
+    c.rollback(1)
+    assert (c.ssm, c.conv, c.offset, c.ssm_prev) == ("s0", "c0", 4, None)

@@ -1,0 +1,251 @@
+"""Parity of the CUDA kernels (through the C ABI) with the CPU oracle and the golden
+fixtures made from the reference's own code.
+
+Tolerances: bit-exact for codes, packed words, bf16 scales/biases and dequantised
+values; bf16 matmul outputs rel-L2 <= 1e-3 against the oracle's bf16 output;
+gated-DeltaNet y (bf16) rel-L2 <= 1e-3 and fp32 states rel-L2 <= 1e-4.
+"""
+import numpy as np
+import pytest
+import torch
+
+import detrand
+import oracle as O
+from make_golden import gd_inputs, qmv_inputs
+
+pytestmark = pytest.mark.gpu
+
+MATMUL_TOL = 1e-3
+STATE_TOL = 1e-4
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if a.dtype == np.uint16:
+        t = t.view(torch.bfloat16)
+    elif a.dtype == np.uint32:
+        t = t.view(torch.int32)
+    return t.cuda()
+
+
+def host_u16(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def rel_l2(a, b):
+    a = O.bf16_to_f32(a).astype(np.float64) if a.dtype == np.uint16 else a.astype(np.float64)
+    b = O.bf16_to_f32(b).astype(np.float64) if b.dtype == np.uint16 else b.astype(np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def qvex():
+    import qvex as q
+    from qvex.build import build
+    build()
+    q.load_library()
+    return q
+
+
+# ------------------------------------------------------------------ qmv (M <= 8)
+
+@pytest.mark.parametrize("name", sorted(p.name for p in __import__("conftest").GOLDEN.glob("qmv_*.npz")))
+def test_qmv_matches_reference_kernel_fixture(qvex, golden_dir, name):
+    z = np.load(golden_dir / name)
+    y = qvex.quantized_matmul(dev(z["x"]), dev(z["w"]), dev(z["scales"]), dev(z["biases"]))
+    torch.cuda.synchronize()
+    assert rel_l2(host_u16(y), z["y"]) <= MATMUL_TOL
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("N,K", [(12288, 4096), (4096, 12288), (67, 64), (1, 128), (1000, 2048), (33, 16384)])
+def test_qmv_matches_oracle(qvex, M, N, K):
+    x, _, w, s, b = qmv_inputs(M, K, N, seed=M * 1000 + N + K)
+    ref = O.qmm_exact(x, w, s, b)
+    y = qvex.quantized_matmul(dev(x), dev(w), dev(s), dev(b))
+    torch.cuda.synchronize()
+    assert rel_l2(host_u16(y), ref) <= MATMUL_TOL
+
+
+def test_qmv_quantized_from_real_weights(qvex):
+    # config-2 style weights (N(0, 0.02) quantized), M = 2 verify shape
+    w = O.f32_to_bf16(detrand.normal((512, 4096), 21) * 0.02)
+    wq, s, b = O.quantize(w, 64, "minmax")
+    x = O.f32_to_bf16(detrand.normal((2, 4096), 22))
+    ref = O.qmm_exact(x, wq, s, b)
+    y = qvex.quantized_matmul(dev(x), dev(wq), dev(s), dev(b))
+    assert rel_l2(host_u16(y), ref) <= MATMUL_TOL
+
+
+def test_qmv_leading_dims_and_out(qvex):
+    x, _, w, s, b = qmv_inputs(4, 1024, 96, seed=5)
+    ref = O.qmm_exact(x, w, s, b)
+    out = torch.empty(2, 2, 96, dtype=torch.bfloat16, device="cuda")
+    y = qvex.quantized_matmul(dev(x).view(2, 2, 1024), dev(w), dev(s), dev(b), out=out)
+    assert y.data_ptr() == out.data_ptr()
+    assert rel_l2(host_u16(y.reshape(4, 96)), ref) <= MATMUL_TOL
+
+
+def test_qmv_multi_alias_and_qlinear(qvex):
+    x, _, w, s, b = qmv_inputs(2, 4096, 300, seed=8)
+    ref = O.qmm_exact(x, w, s, b)
+    y1 = qvex.qmv_multi(dev(x), dev(w), dev(s), dev(b))
+    lin = qvex.QLinear(dev(w), dev(s), dev(b), 64, 4)
+    y2 = lin(dev(x))
+    assert torch.equal(y1, y2)
+    assert rel_l2(host_u16(y1), ref) <= MATMUL_TOL
+
+
+def test_qlinear_fuse_equals_separate(qvex):
+    parts = [qmv_inputs(1, 1024, n, seed=40 + n) for n in (96, 32, 8)]
+    x = dev(parts[0][0])
+    lins = [qvex.QLinear(dev(p[2]), dev(p[3]), dev(p[4])) for p in parts]
+    fused = qvex.QLinear.fuse(lins)
+    y = fused(x)
+    sep = torch.cat([l(x) for l in lins], dim=-1)
+    assert torch.equal(y, sep)
+
+
+# ------------------------------------------------------------------ quantize / dequantize
+
+@pytest.mark.parametrize("variant", ["minmax", "zero_exact"])
+def test_quantize_bit_exact_config2(qvex, variant):
+    w = O.f32_to_bf16(detrand.normal((12288, 4096), 2) * 0.02)
+    wq_r, s_r, b_r = O.quantize(w, 64, variant)
+    wq, s, b = qvex.quantize(dev(w), 64, 4, variant=variant)
+    torch.cuda.synchronize()
+    assert np.array_equal(wq.view(torch.int32).cpu().numpy().view(np.uint32), wq_r)
+    assert np.array_equal(host_u16(s), s_r)
+    assert np.array_equal(host_u16(b), b_r)
+
+
+@pytest.mark.parametrize("variant", ["minmax", "zero_exact"])
+def test_quantize_edge_cases_bit_exact(qvex, variant):
+    w = (detrand.normal((8, 256), 3) * 0.02).astype(np.float32)
+    w[0] = 0.0
+    w[1] = 3.0
+    w[2, :64] = 1e30
+    w[3, :64] = -1e-38
+    w[4, ::2] = 65504.0
+    w[5] = np.linspace(-1, 1, 256)
+    w[6, :64] = 7.0
+    w[6, 1] = -7.0
+    wb = O.f32_to_bf16(w)
+    wq_r, s_r, b_r = O.quantize(wb, 64, variant)
+    wq, s, b = qvex.quantize(dev(wb), 64, 4, variant=variant)
+    assert np.array_equal(wq.view(torch.int32).cpu().numpy().view(np.uint32), wq_r)
+    assert np.array_equal(host_u16(s), s_r)
+    assert np.array_equal(host_u16(b), b_r)
+
+
+def test_pack_order_on_device(qvex, golden_dir):
+    # quantize a row whose codes are known, compare the packed words with the reference pack
+    z = np.load(golden_dir / "pack_4bit.npz")
+    codes = z["codes"][3:4, :64]                     # 0..15, 0..15, ...
+    w = O.f32_to_bf16(codes.astype(np.float32))     # scale 1, bias 0 under minmax
+    wq, s, b = qvex.quantize(dev(w), 64, 4)
+    assert np.array_equal(wq.view(torch.int32).cpu().numpy().view(np.uint32), z["packed"][3:4, :8])
+
+
+def test_dequantize_bit_exact(qvex):
+    x, _, w, s, b = qmv_inputs(1, 4096, 2048, seed=77)
+    ref = O.dequantize(w, s, b)
+    out = qvex.dequantize(dev(w), dev(s), dev(b))
+    assert np.array_equal(host_u16(out), ref)
+
+
+def test_dequantize_rows_gather(qvex):
+    _, _, w, s, b = qmv_inputs(1, 512, 100, seed=78)
+    ids = np.array([[5, 0, 99], [42, 42, 7]], np.int32)
+    full = O.dequantize(w, s, b)
+    emb = qvex.QEmbedding(dev(w), dev(s), dev(b))
+    out = emb(torch.from_numpy(ids).cuda())
+    assert out.shape == (2, 3, 512)
+    assert np.array_equal(host_u16(out).reshape(6, 512), full[ids.reshape(-1)])
+
+
+def test_dequantize_rows_bad_id_sets_device_status(qvex):
+    from qvex import _lib
+    _, _, w, s, b = qmv_inputs(1, 128, 10, seed=79)
+    _lib.device_status(torch.cuda.current_stream().cuda_stream)  # clear
+    out = qvex.dequantize_rows(dev(w), dev(s), dev(b), torch.tensor([1, 10], dtype=torch.int32, device="cuda"))
+    st = _lib.device_status(torch.cuda.current_stream().cuda_stream)
+    assert st == _lib.QVX_ERR_INVALID
+    assert torch.all(out[1] == 0)
+    assert _lib.device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+# ------------------------------------------------------------------ gated DeltaNet
+
+def run_gd(qvex, q, k, v, a, b, A_log, dt, st, keep_mid):
+    outs = qvex.gated_delta(dev(q), dev(k), dev(v), dev(a), dev(b), torch.from_numpy(A_log).cuda(),
+                            torch.from_numpy(dt).cuda(), torch.from_numpy(st).cuda(), keep_mid=keep_mid)
+    torch.cuda.synchronize()
+    return [host_u16(outs[0])] + [o.cpu().numpy() for o in outs[1:]]
+
+
+@pytest.mark.parametrize("name", sorted(p.name for p in __import__("conftest").GOLDEN.glob("gd_b*.npz")))
+def test_gated_delta_matches_reference_kernel_fixture(qvex, golden_dir, name):
+    z = np.load(golden_dir / name)
+    mid = "state_mid" in z.files
+    out = run_gd(qvex, z["q"], z["k"], z["v"], z["a"], z["b"], z["A_log"], z["dt_bias"], z["state"], mid)
+    assert rel_l2(out[0], z["y"]) <= MATMUL_TOL
+    assert rel_l2(out[1], z["state_out"]) <= STATE_TOL
+    if mid:
+        assert rel_l2(out[2], z["state_mid"]) <= STATE_TOL
+
+
+@pytest.mark.parametrize("kind", ["zeros", "normal"])
+def test_gated_delta_qwen35_fixture(qvex, golden_dir, kind):
+    z = np.load(golden_dir / f"gd_qwen35_t4_{kind}.npz")
+    q, k, v, a, b, st = gd_inputs(1, 4, 16, 32, 128, 128, int(z["seed"]), kind)
+    zeros = np.zeros(32, np.float32)
+    y, so, sm = run_gd(qvex, q, k, v, a, b, zeros, zeros, st, True)
+    assert rel_l2(y, z["y"]) <= MATMUL_TOL
+    assert rel_l2(so.reshape(-1)[::4099], z["state_out_sample"]) <= STATE_TOL
+
+
+@pytest.mark.parametrize("B,T,kind", [(1, 1, "normal"), (8, 1, "normal"), (1, 2048, "zeros"), (8, 64, "normal"),
+                                      (2, 2, "zeros")])
+def test_gated_delta_config3_vs_oracle(qvex, B, T, kind):
+    q, k, v, a, b, st = gd_inputs(B, T, 16, 32, 128, 128, 900 + B + T, kind)
+    zeros = np.zeros(32, np.float32)
+    ry, rs = O.gated_delta(q, k, v, a, b, zeros, zeros, st)
+    y, so = run_gd(qvex, q, k, v, a, b, zeros, zeros, st, False)
+    assert rel_l2(y, ry) <= MATMUL_TOL
+    assert rel_l2(so, rs) <= STATE_TOL
+
+
+def test_gated_delta_snapshot_rollback(qvex):
+    """Config 3: 4 steps with the snapshot; state_mid must equal the state after 3 steps
+    from the same kernel (bitwise) and re-running step 4 from it must reproduce state_out."""
+    q, k, v, a, b, st = gd_inputs(1, 4, 16, 32, 128, 128, 1234, "normal")
+    zeros = np.zeros(32, np.float32)
+    y4, s4, mid = run_gd(qvex, q, k, v, a, b, zeros, zeros, st, True)
+    y3, s3 = run_gd(qvex, q[:, :3], k[:, :3], v[:, :3], a[:, :3], b[:, :3], zeros, zeros, st, False)
+    assert np.array_equal(mid, s3)
+    assert np.array_equal(y4[:, :3], y3)
+    y_last, s_again = run_gd(qvex, q[:, 3:], k[:, 3:], v[:, 3:], a[:, 3:], b[:, 3:], zeros, zeros, mid, False)
+    assert np.array_equal(s_again, s4)
+    assert np.array_equal(y_last[:, 0], y4[:, 3])
+
+
+def test_gated_delta_gates_and_gqa_dk64(qvex):
+    q, k, v, a, b, st = gd_inputs(2, 9, 2, 8, 64, 32, 55, "normal")
+    A_log = (detrand.normal((8,), 56) * 0.5).astype(np.float32)
+    dt = (detrand.normal((8,), 57) * 3.0).astype(np.float32)  # softplus linear branch (x > 20) is reached
+    a = O.f32_to_bf16(O.bf16_to_f32(a) * 12.0)
+    ry, rs, rm = O.gated_delta(q, k, v, a, b, A_log, dt, st, keep_mid=True)
+    y, so, sm = run_gd(qvex, q, k, v, a, b, A_log, dt, st, True)
+    assert rel_l2(y, ry) <= MATMUL_TOL
+    assert rel_l2(so, rs) <= STATE_TOL and rel_l2(sm, rm) <= STATE_TOL
+
+
+def test_gated_delta_in_place_state(qvex):
+    q, k, v, a, b, st = gd_inputs(1, 3, 16, 32, 128, 128, 77, "normal")
+    zeros = torch.zeros(32, device="cuda")
+    state = torch.from_numpy(st).cuda()
+    y1, s1 = qvex.gated_delta(dev(q), dev(k), dev(v), dev(a), dev(b), zeros, zeros, state)
+    y2, s2 = qvex.gated_delta(dev(q), dev(k), dev(v), dev(a), dev(b), zeros, zeros, state, out_state=state)
+    assert s2.data_ptr() == state.data_ptr()
+    assert torch.equal(s1, s2) and torch.equal(y1, y2)
