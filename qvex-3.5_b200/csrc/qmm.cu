@@ -10,14 +10,19 @@
 // (no overflow, full fp16 precision); the epilogue multiplies by 2^e[m].
 //
 // Workspace layout (256-byte aligned sections):
-//   [0]            x16   fp16  [M, K]
+//   [0]            x16   fp16  [M, K]   x * 2^-e[m], inputs stored in the order
+//                                        (k, k+4) within every 8 (the order the weight
+//                                        dequantiser produces pairs in)
 //   [off_exp]      e     int32 [M]
+//   [off_fexp]     f     int32 [N]     per weight row exponent
+//   [off_prm]      prm   uint2 [N, K/64] per group fp16 multipliers (S24, S20 | B)
 #include "common.cuh"
 
 namespace qvx {
 
-int qmm_tc_launch(const __half* x16, const int32_t* xexp, const uint32_t* w, const uint16_t* sc,
-                  const uint16_t* bi, __nv_bfloat16* y, int M, int N, int K, cudaStream_t stream);
+int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, const uint2* prm, const uint32_t* w,
+                  __nv_bfloat16* y, int M, int N, int K, cudaStream_t stream);
+int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm, int N, int K, cudaStream_t stream);
 int qmv_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
                 int K, cudaStream_t stream);
 int check_qparams(const char* who, const void* x, const uint32_t* w, const void* s, const void* b, const void* y,
@@ -26,14 +31,16 @@ int check_qparams(const char* who, const void* x, const uint32_t* w, const void*
 static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct QmmWorkspace {
-  size_t off_x16, off_exp, total;
+  size_t off_x16, off_exp, off_fexp, off_prm, total;
 };
 
-static QmmWorkspace qmm_ws_layout(int M, int K) {
+static QmmWorkspace qmm_ws_layout(int M, int N, int K) {
   QmmWorkspace l;
   l.off_x16 = 0;
   l.off_exp = align256((size_t)M * K * sizeof(__half));
-  l.total = l.off_exp + align256((size_t)M * sizeof(int32_t));
+  l.off_fexp = l.off_exp + align256((size_t)M * sizeof(int32_t));
+  l.off_prm = l.off_fexp + align256((size_t)N * sizeof(int32_t));
+  l.total = l.off_prm + align256((size_t)N * (K / 64) * sizeof(uint2));
   return l;
 }
 
@@ -76,11 +83,16 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const __nv_bfloat16* __re
   for (int i = threadIdx.x; i < n16; i += blockDim.x) {
     const uint4 t = xr[i];
     const uint32_t u[4] = {t.x, t.y, t.z, t.w};
-    uint32_t o[4];
+    float xf[8];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const __half2 p = __floats2half2_rn(__uint_as_float(u[h] << 16) * scale,
-                                          __uint_as_float(u[h] & 0xffff0000u) * scale);
+      xf[2 * h] = __uint_as_float(u[h] << 16) * scale;
+      xf[2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u) * scale;
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {  // pairs (x_h, x_{h+4})
+      const __half2 p = __floats2half2_rn(xf[h], xf[h + 4]);
       o[h] = *reinterpret_cast<const uint32_t*>(&p);
     }
     outr[2 * i] = make_uint2(o[0], o[1]);
@@ -91,7 +103,7 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const __nv_bfloat16* __re
 
 int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
                 int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  const QmmWorkspace l = qmm_ws_layout(M, K);
+  const QmmWorkspace l = qmm_ws_layout(M, N, K);
   if (!workspace || workspace_bytes < l.total)
     return fail(QVX_ERR_WORKSPACE, "qvx_qmm: workspace of %zu bytes needed, %zu given", l.total,
                 workspace ? workspace_bytes : (size_t)0);
@@ -99,19 +111,21 @@ int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void
   char* ws = static_cast<char*>(workspace);
   __half* x16 = reinterpret_cast<__half*>(ws + l.off_x16);
   int32_t* xexp = reinterpret_cast<int32_t*>(ws + l.off_exp);
+  int32_t* fexp = reinterpret_cast<int32_t*>(ws + l.off_fexp);
+  uint2* prm = reinterpret_cast<uint2*>(ws + l.off_prm);
   x_to_f16_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), x16, xexp, K);
   int rc = check_launch("qvx_qmm prepass");
   if (rc) return rc;
-  return qmm_tc_launch(x16, xexp, w, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
-                       static_cast<__nv_bfloat16*>(y), M, N, K, stream);
+  rc = qmm_w_prep(scales, biases, fexp, prm, N, K, stream);
+  if (rc) return rc;
+  return qmm_tc_launch(x16, xexp, fexp, prm, w, static_cast<__nv_bfloat16*>(y), M, N, K, stream);
 }
 
 }  // namespace qvx
 
 extern "C" size_t qvx_qmm_workspace_size(int M, int N, int K) {
-  (void)N;
-  if (M < 1 || K < 1) return 0;
-  return qvx::qmm_ws_layout(M, K).total;
+  if (M < 1 || N < 1 || K < 64) return 0;
+  return qvx::qmm_ws_layout(M, N, K).total;
 }
 
 extern "C" int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M,

@@ -251,8 +251,14 @@ static int launch_qmv(const void* x, const uint32_t* w, const void* s, const voi
   return QVX_OK;
 }
 
+int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
+                   cudaStream_t stream);
+
 int qmv_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
                 int M, int N, int K, cudaStream_t stream) {
+  // the streaming kernel (qmv_stream.cu) covers K % 512 == 0; this file's kernel the rest
+  const int rc = qmv_stream_try(x, w, scales, biases, y, M, N, K, stream);
+  if (rc >= 0) return rc;
   QmvPlan pl;
   if (!plan_qmv(M, K, &pl)) return fail(QVX_ERR_UNSUPPORTED, "qvx_qmv: K=%d too large for M=%d", K, M);
 #define QVX_QMV_CASE(MC_, LEN_) \

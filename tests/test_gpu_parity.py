@@ -249,3 +249,101 @@ def test_gated_delta_in_place_state(qvex):
     y2, s2 = qvex.gated_delta(dev(q), dev(k), dev(v), dev(a), dev(b), zeros, zeros, state, out_state=state)
     assert s2.data_ptr() == state.data_ptr()
     assert torch.equal(s1, s2) and torch.equal(y1, y2)
+
+
+# ------------------------------------------------------------------ qmm (tensor cores, M > 8)
+
+def qmm_direct(qvex, x, w, s, b):
+    """Call qvx_qmm through the C ABI for any M (including M <= 8)."""
+    import ctypes
+    from qvex import _lib
+    M, K = x.shape
+    N = w.shape[0]
+    xd, wd, sd, bd = dev(x), dev(w), dev(s), dev(b)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    need = _lib.lib().qvx_qmm_workspace_size(M, N, K)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    P = ctypes.c_void_p
+    rc = _lib.lib().qvx_qmm(P(xd.data_ptr()), P(wd.data_ptr()), P(sd.data_ptr()), P(bd.data_ptr()),
+                            P(y.data_ptr()), M, N, K, 64, 4, P(ws.data_ptr()), need,
+                            P(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc, "qvx_qmm")
+    torch.cuda.synchronize()
+    return host_u16(y)
+
+
+@pytest.mark.parametrize("M,N,K", [(9, 256, 64), (16, 256, 1024), (64, 1024, 4096), (100, 300, 512),
+                                   (129, 520, 1024), (256, 257, 2048), (512, 4096, 4096), (37, 12288, 4096),
+                                   (200, 4096, 12288)])
+def test_qmm_matches_oracle(qvex, M, N, K):
+    x, _, w, s, b = qmv_inputs(M, K, N, seed=7 * M + N + K)
+    ref = O.qmm_exact(x, w, s, b)
+    y = qvex.quantized_matmul(dev(x), dev(w), dev(s), dev(b))
+    torch.cuda.synchronize()
+    assert rel_l2(host_u16(y), ref) <= MATMUL_TOL
+
+
+@pytest.mark.parametrize("M", [1, 2, 5, 8])
+def test_qmm_small_m_direct(qvex, M):
+    x, _, w, s, b = qmv_inputs(M, 2048, 384, seed=300 + M)
+    ref = O.qmm_exact(x, w, s, b)
+    assert rel_l2(qmm_direct(qvex, x, w, s, b), ref) <= MATMUL_TOL
+
+
+def test_qmm_config2_full_size_sampled(qvex):
+    """Config 2: W ~ N(0, 0.02) [12288, 4096] quantised, x ~ N(0,1) [2048, 4096]; the
+    oracle checks every 16th token row (all 12288 outputs of each)."""
+    W = O.f32_to_bf16(detrand.normal((12288, 4096), 2) * 0.02)
+    wq, s, b = O.quantize(W, 64, "minmax")
+    x = O.f32_to_bf16(detrand.normal((2048, 4096), 3))
+    y = qvex.quantized_matmul(dev(x), dev(wq), dev(s), dev(b))
+    torch.cuda.synchronize()
+    yh = host_u16(y)
+    ref = O.qmm_exact(x[::16], wq, s, b)
+    assert rel_l2(yh[::16], ref) <= MATMUL_TOL
+    assert np.isfinite(O.bf16_to_f32(yh)).all()
+
+
+def test_qmm_dynamic_range(qvex):
+    """Token rows and weight rows whose magnitudes differ by many orders: the per-row
+    power-of-two scaling keeps fp16 operands in range without losing precision."""
+    M, N, K = 48, 320, 1024
+    x = detrand.normal((M, K), 5)
+    x[0] *= 3e4      # would overflow fp16 unscaled
+    x[1] *= 1e-6     # would underflow
+    x[2] = 0.0       # all-zero row
+    xb = O.f32_to_bf16(x)
+    W = detrand.normal((N, K), 6) * 0.02
+    W[0] *= 1e3
+    W[1] *= 1e-5
+    W[2, :64] = 0.0
+    wq, s, b = O.quantize(O.f32_to_bf16(W), 64, "minmax")
+    ref = O.qmm_exact(xb, wq, s, b)
+    y = host_u16(qvex.quantized_matmul(dev(xb), dev(wq), dev(s), dev(b)))
+    r = O.bf16_to_f32(ref).astype(np.float64)
+    g = O.bf16_to_f32(y).astype(np.float64)
+    assert np.all(g[2] == 0)
+    # per token row relative error (row scales differ by 1e10)
+    for m in (0, 1, 3):
+        assert np.linalg.norm(g[m] - r[m]) / np.linalg.norm(r[m]) <= MATMUL_TOL
+    # per weight row
+    for n in (0, 1, 5):
+        assert np.linalg.norm(g[:, n] - r[:, n]) / np.linalg.norm(r[:, n]) <= 2 * MATMUL_TOL
+
+
+def test_qmm_and_qmv_agree(qvex):
+    x, _, w, s, b = qmv_inputs(8, 4096, 1024, seed=99)
+    y_qmv = host_u16(qvex.quantized_matmul(dev(x), dev(w), dev(s), dev(b)))
+    y_qmm = qmm_direct(qvex, x, w, s, b)
+    assert rel_l2(y_qmm, y_qmv) <= MATMUL_TOL
+
+
+def test_qmm_workspace_reuse_and_out(qvex):
+    x, _, w, s, b = qmv_inputs(64, 1024, 512, seed=4)
+    ref = O.qmm_exact(x, w, s, b)
+    need = qvex.qmm_workspace_size(64, 512, 1024)
+    ws = torch.empty(need + 4096, dtype=torch.uint8, device="cuda")
+    out = torch.empty(64, 512, dtype=torch.bfloat16, device="cuda")
+    for _ in range(2):
+        qvex.quantized_matmul(dev(x), dev(w), dev(s), dev(b), out=out, workspace=ws)
+    assert rel_l2(host_u16(out), ref) <= MATMUL_TOL
