@@ -2,43 +2,54 @@
 //
 // Same contract as qmv.cu (y[M,N] = x[M,K] @ dequant(w)^T, replacing mx.quantized_matmul
 // at M = 1..8, engine/model.py:87-91, and qmv_multi, engine/kernels.py:132-211), built so
-// that bytes in flight do not cost registers:
+// that bytes in flight do not cost registers and consecutive launches overlap:
 //
-//   * warp P (producer) streams blocks of R whole rows -- codes (R*K/2 contiguous bytes),
-//     scales and biases (R*K/32 bytes each) -- into an S-stage shared-memory ring with
-//     cp.async.bulk, completion counted on an mbarrier.  It starts before
-//     griddepcontrol.wait: weights do not depend on the upstream kernel, so the ring
-//     fills while the previous launch drains.
-//   * warps 0..P-1 (compute) each own a 1024-wide slice of K: lane l holds x for the 32
-//     inputs [1024p + 32l, +32) of MC tokens in registers for the whole launch.  Per
-//     stage a lane reads 16 bytes of codes per row (conflict-free LDS.128) and the row's
-//     scale/bias for its group.
-//   * warp P+1 (reducer) adds the P per-warp partials of each (row, token) and writes
-//     bf16 y, then releases the stage.
+//   * warp W-2 (producer) streams blocks of R whole rows -- codes (R*K/2 contiguous
+//     bytes), scales and biases (R*K/32 bytes each) -- into an 8-stage shared-memory ring
+//     with cp.async.bulk, completion counted on an mbarrier.  It runs before
+//     griddepcontrol.wait: weights do not depend on the upstream kernel.
+//   * one CTA per SM using under half of the SM, so with programmatic dependent launch the
+//     NEXT projection's CTA is already resident and its producer fills its own ring while
+//     this one computes: HBM stays busy across launch boundaries.
+//   * compute warps form T teams of P = K/1024 warps; team t owns rows t*RT..t*RT+RT-1 of
+//     every stage, and lane l of warp p of a team owns the 32 inputs
+//     [1024p + 32l, +32) of K (one conflict-free LDS.128 of codes per row).
+//   * warp W-1 (reducer) adds the P per-warp partials of each (row, token), writes bf16 y
+//     and releases the stage.
 //
-// Dequant arithmetic.  For the nibble pair (i, i+1) of a word, one shift puts nibble i at
-// mantissa bits 15..18 and nibble i+1 at bits 19..22 of 1.0f; two LOP3s yield
-// f_lo = 1 + q_i/256 and f_hi = 1 + q_{i+1}/16, and one fma.rn.f32x2 accumulates both
-// against (x_i, x_{i+1}).  With d_lo = sum f_lo x, d_hi = sum f_hi x over the even / odd
-// inputs and xs_lo, xs_hi the matching sums of x, the group term of the reference
-// factorisation s*sum(q x) + b*sum(x) (engine/kernels.py:151-171) is
-//   256 s d_lo + 16 s d_hi + (b - 256 s) xs_lo + (b - 16 s) xs_hi.
-// That is 2 instructions per code for one token (shift+2 LOP3 per pair, one FFMA2 per
-// pair), fp32 throughout.
+// Arithmetic: exact integer dot products.  Instruction rates measured on B200 put LOP3,
+// SHF and DP4A at half rate on separate pipes, with DP4A-based unpacking sustaining ~75
+// codes/clk/SM against ~43 for mixed fp16 FMA and ~25 for fp32 bit tricks.  So:
+//   * a lane's 32 inputs of one token become 24-bit fixed point against the slice max
+//     (x_fix = rint(x * 2^(23-E)), 2^(E-1) <= max|x| < 2^E, exact for every bf16 value
+//     within 2^15 of the max), split into byte planes p0, p1 (unsigned) and p2 (signed),
+//     packed four inputs per register in the order the codes unpack;
+//   * a packed word w gives its even codes as bytes with one LOP3 (w & 0x0F0F0F0F) and its
+//     odd codes with a shift and a LOP3; three DP4As per 4 codes accumulate
+//     sum q * p_j in int32 (no overflow: 15*255*32 < 2^17);
+//   * per row: Q = a0 + 256 a1 + 65536 a2, sum(q x) = 2^(E-23) Q, and the group term of the
+//     reference factorisation s*sum(q x) + b*sum(x) (engine/kernels.py:151-171).
 #include "sm100.cuh"
 
 namespace qvx {
 
-constexpr int kStreamStages = 4;
+constexpr int kStreamMaxComputeWarps = 12;
+// Shared memory per CTA: kept under half of the SM so that two launches are co-resident.
+constexpr size_t kStreamSmemBudget = 105 * 1024;
+constexpr int kStreamMaxStages = 8;
+// Codes per stage: measured on B200, 16 KB stages (4 rows per team at K = 4096) stream
+// lm_head at ~80% of HBM against ~63% for 8 KB stages.
+constexpr size_t kStreamStageCodeBytes = 16384;
 
-template <int MC, int R>
-struct StreamCfg {
-  static constexpr int V = R * MC <= 1 ? 1 : R * MC <= 2 ? 2 : R * MC <= 4 ? 4 : R * MC <= 8 ? 8 : 16;
-  static constexpr int LV = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : 4;
+template <int NV>
+struct VCfg {
+  static constexpr int V = NV <= 1 ? 1 : NV <= 2 ? 2 : NV <= 4 ? 4 : NV <= 8 ? 8 : NV <= 16 ? 16 : 32;
+  static constexpr int LV = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5;
 };
 
-__host__ __device__ inline size_t stream_stage_bytes(int R, int K, int P) {
-  return (size_t)R * K / 2 + (size_t)R * K / 16 + 128u * P;  // codes, scales+biases, partials
+__host__ __device__ inline size_t stream_stage_bytes(int R, int K) {
+  // codes, scales + biases, per-warp partials (32 floats each)
+  return (size_t)R * K / 2 + (size_t)R * K / 16 + 128u * kStreamMaxComputeWarps;
 }
 
 template <int V, int OFF>
@@ -60,32 +71,72 @@ __device__ __forceinline__ void reduce_transpose(float* p, int lane) {
   }
 }
 
-// f_lo = 1 + q_i/256, f_hi = 1 + q_{i+1}/16 for the nibble pair starting at nibble I (even).
-template <int I>
-__device__ __forceinline__ unsigned long long nib_pair(uint32_t w) {
-  constexpr int sh = 15 - 4 * I;
-  const uint32_t t = sh >= 0 ? (w << sh) : (w >> (-sh));
-  const uint32_t lo = (t & 0x00078000u) | 0x3F800000u;
-  const uint32_t hi = (t & 0x00780000u) | 0x3F800000u;
-  return (unsigned long long)lo | ((unsigned long long)hi << 32);
+__device__ __forceinline__ uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
-template <int MC, int R>
-__global__ void __launch_bounds__(512) qmv_stream_kernel(const __nv_bfloat16* __restrict__ x,
-                                                          const uint32_t* __restrict__ w,
-                                                          const uint16_t* __restrict__ sc,
-                                                          const uint16_t* __restrict__ bi,
-                                                          __nv_bfloat16* __restrict__ y, int M, int N, int K,
-                                                          int* status) {
-  using C = StreamCfg<MC, R>;
-  constexpr int S = kStreamStages;
-  constexpr int V = C::V, LV = C::LV;
+// x planes of one token for a lane's 32 inputs: pl[j][2*w + h] packs, for packed word w
+// (inputs 8w..8w+7), the plane-j bytes of inputs 8w+h, 8w+h+2, 8w+h+4, 8w+h+6.
+struct XPlanes {
+  uint32_t pl[3][8];
+  float scale;  // 2^(E-23)
+  float xsum;   // sum of the 32 inputs
+};
+
+__device__ __forceinline__ void make_planes(const float (&xf)[32], XPlanes& xp) {
+  float mx = 0.0f, sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    mx = fmaxf(mx, fabsf(xf[i]));
+    sum += xf[i];
+  }
+  int E = 0;
+  if (mx > 0.0f && isfinite(mx)) frexpf(mx, &E);  // 2^(E-1) <= mx < 2^E
+  E = max(E, -100);
+  const float up = ldexpf(1.0f, 23 - E);
+  xp.scale = ldexpf(1.0f, E - 23);
+  xp.xsum = sum;
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int v = __float2int_rn(xf[8 * w + h + 2 * i] * up);  // |v| < 2^23
+        b0 |= ((uint32_t)v & 0xFFu) << (8 * i);
+        b1 |= (((uint32_t)v >> 8) & 0xFFu) << (8 * i);
+        b2 |= (((uint32_t)v >> 16) & 0xFFu) << (8 * i);
+      }
+      xp.pl[0][2 * w + h] = b0;
+      xp.pl[1][2 * w + h] = b1;
+      xp.pl[2][2 * w + h] = b2;
+    }
+}
+
+template <int MC, int RT, bool FULLK, int S>
+__global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
+    qmv_stream_kernel(const __nv_bfloat16* __restrict__ x, const uint32_t* __restrict__ w,
+                      const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, __nv_bfloat16* __restrict__ y,
+                      int M, int N, int K, int T, int* status) {
+  using VC = VCfg<RT * MC>;
+  constexpr int V = VC::V, LV = VC::LV;
   extern __shared__ __align__(128) uint8_t smem[];
 
-  const int P = (blockDim.x >> 5) - 2;  // compute warps
+  const int NW = blockDim.x >> 5;          // warps
+  const int CW = NW - 2;                   // compute warps = T * P
+  const int P = CW / T;                    // warps per team
+  const int R = T * RT;                    // rows per stage
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = K >> 6;
-  const size_t stage_bytes = stream_stage_bytes(R, K, P);
+  const size_t stage_bytes = stream_stage_bytes(R, K);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* done = full + S;
   uint64_t* empty = done + S;
@@ -100,7 +151,7 @@ __global__ void __launch_bounds__(512) qmv_stream_kernel(const __nv_bfloat16* __
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&done[s], P);
+      mbar_init(&done[s], CW);
       mbar_init(&empty[s], 1);
     }
     *abort_flag = 0;
@@ -111,7 +162,7 @@ __global__ void __launch_bounds__(512) qmv_stream_kernel(const __nv_bfloat16* __
 
   auto stage = [&](int s) { return smem + (size_t)s * stage_bytes; };
 
-  if (warp == P) {
+  if (warp == NW - 2) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int c = 0;
@@ -131,81 +182,85 @@ __global__ void __launch_bounds__(512) qmv_stream_kernel(const __nv_bfloat16* __
       // let every copy already issued land before the CTA can exit
       for (int j = max(0, c - S); j < c; ++j) mbar_wait_drain(&full[j % S], (uint32_t)(j / S) & 1u, status);
     }
-  } else if (warp < P) {
+  } else if (warp < CW) {
     // ------------------------------------------------------------ compute
-    const int k0 = warp * 1024 + lane * 32;
-    const bool kact = k0 < K;
-    const int g = k0 >> 6;
+    const int team = warp / P, wt = warp % P;
+    const int k0 = wt * 1024 + lane * 32;
+    const bool kact = FULLK || k0 < K;
+    const int g = kact ? (k0 >> 6) : 0;
     pdl_wait();  // x comes from the upstream kernel
-    unsigned long long xp[MC][16];
-    float xs_lo[MC], xs_hi[MC];
+    XPlanes xp[MC];
 #pragma unroll
     for (int m = 0; m < MC; ++m) {
-      xs_lo[m] = 0.0f;
-      xs_hi[m] = 0.0f;
       const bool live = kact && m < mc;
-      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(m0 + (live ? m : 0)) * K + (kact ? k0 : 0));
+      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(m0 + (live ? m : 0)) * K + (live ? k0 : 0));
+      float xf[32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint4 t = live ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
         const uint32_t u[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
-          const float lo = __uint_as_float(u[h] << 16), hi = __uint_as_float(u[h] & 0xffff0000u);
-          xp[m][c * 4 + h] = pack_f32x2(lo, hi);
-          xs_lo[m] += lo;
-          xs_hi[m] += hi;
+          xf[c * 8 + 2 * h] = __uint_as_float(u[h] << 16);
+          xf[c * 8 + 2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
         }
       }
+      make_planes(xf, xp[m]);
     }
     for (int c = 0; c < nchunks; ++c) {
-      const int s = c % S;
+      const int s_ = c % S;
       const uint32_t ph = (uint32_t)(c / S) & 1u;
-      if (!mbar_wait(&full[s], ph, abort_flag, status)) break;
-      const int nr = min(R, r_end - (r_begin + c * R));
-      const uint8_t* st = stage(s);
+      if (!mbar_wait(&full[s_], ph, abort_flag, status)) break;
+      const uint8_t* st = stage(s_);
       const uint16_t* ssc = reinterpret_cast<const uint16_t*>(st + (size_t)R * K / 2);
       const uint16_t* sbi = ssc + (size_t)R * G;
       float pv[V];
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        uint4 cw = make_uint4(0, 0, 0, 0);
-        float sf = 0.0f, bf = 0.0f;
-        if (kact && r < nr) {
-          cw = *reinterpret_cast<const uint4*>(st + (size_t)r * (K / 2) + (k0 >> 1));
-          sf = bf16_bits_to_f32(ssc[r * G + g]);
-          bf = bf16_bits_to_f32(sbi[r * G + g]);
-        }
-        const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
-        unsigned long long d[MC];
+      for (int i = 0; i < V; ++i) pv[i] = 0.0f;
+      // rows past the end of the CTA's range compute on stale shared memory; the reducer
+      // never stores them
 #pragma unroll
-        for (int m = 0; m < MC; ++m) d[m] = 0ull;
+      for (int i = 0; i < RT; ++i) {
+        const int r = team * RT + i;
+        const uint4 cw = *reinterpret_cast<const uint4*>(st + (size_t)r * (K / 2) + (kact ? (k0 >> 1) : 0));
+        const float sf = bf16_bits_to_f32(ssc[r * G + g]);
+        const float bf = bf16_bits_to_f32(sbi[r * G + g]);
+        const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
+        uint32_t lo[4], hi[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const unsigned long long f0 = nib_pair<0>(wd[j]), f1 = nib_pair<2>(wd[j]);
-          const unsigned long long f2 = nib_pair<4>(wd[j]), f3 = nib_pair<6>(wd[j]);
-#pragma unroll
-          for (int m = 0; m < MC; ++m) {
-            d[m] = fma_f32x2(f0, xp[m][4 * j + 0], d[m]);
-            d[m] = fma_f32x2(f1, xp[m][4 * j + 1], d[m]);
-            d[m] = fma_f32x2(f2, xp[m][4 * j + 2], d[m]);
-            d[m] = fma_f32x2(f3, xp[m][4 * j + 3], d[m]);
-          }
+          lo[j] = wd[j] & 0x0F0F0F0Fu;          // codes 8j + 0, 2, 4, 6
+          hi[j] = (wd[j] >> 4) & 0x0F0F0F0Fu;   // codes 8j + 1, 3, 5, 7
         }
-        const float s256 = 256.0f * sf, s16 = 16.0f * sf;
-        const float c_lo = bf - s256, c_hi = bf - s16;
 #pragma unroll
-        for (int m = 0; m < MC; ++m)
-          pv[r * MC + m] =
-              fmaf(s256, f32x2_lo(d[m]), fmaf(s16, f32x2_hi(d[m]), fmaf(c_lo, xs_lo[m], c_hi * xs_hi[m])));
+        for (int m = 0; m < MC; ++m) {
+          // six independent chains (plane x even/odd codes), four DP4As deep
+          uint32_t a0l = 0, a1l = 0, a0h = 0, a1h = 0;
+          int a2l = 0, a2h = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            a0l = dp4a_uu(lo[j], xp[m].pl[0][2 * j], a0l);
+            a1l = dp4a_uu(lo[j], xp[m].pl[1][2 * j], a1l);
+            a2l = dp4a_us(lo[j], xp[m].pl[2][2 * j], a2l);
+            a0h = dp4a_uu(hi[j], xp[m].pl[0][2 * j + 1], a0h);
+            a1h = dp4a_uu(hi[j], xp[m].pl[1][2 * j + 1], a1h);
+            a2h = dp4a_us(hi[j], xp[m].pl[2][2 * j + 1], a2h);
+          }
+          // |a| < 2^22: int -> float by the 1.5 * 2^23 magic number, exactly and off the XU pipe
+          const float f0 = __int_as_float(0x4B400000 + (int)(a0l + a0h)) - 12582912.0f;
+          const float f1 = __int_as_float(0x4B400000 + (int)(a1l + a1h)) - 12582912.0f;
+          const float f2 = __int_as_float(0x4B400000 + (a2l + a2h)) - 12582912.0f;
+          const float q = fmaf(f2, 65536.0f, fmaf(f1, 256.0f, f0));  // sum q * x_fix
+          const float part = fmaf(sf * xp[m].scale, q, bf * xp[m].xsum);
+          pv[i * MC + m] = FULLK ? part : (kact ? part : 0.0f);
+        }
       }
-#pragma unroll
-      for (int i = R * MC; i < V; ++i) pv[i] = 0.0f;
       reduce_transpose<V, 16>(pv, lane);
       float* red = reinterpret_cast<float*>(const_cast<uint8_t*>(st) + (size_t)R * K / 2 + (size_t)R * K / 16);
-      if ((lane & ((32 >> LV) - 1)) == 0) red[warp * 32 + (lane >> (5 - LV))] = pv[0];
+      if ((lane & ((32 >> LV) - 1)) == 0 && (lane >> (5 - LV)) < RT * MC)
+        red[warp * 32 + (lane >> (5 - LV))] = pv[0];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&done[s]);
+      if (lane == 0) mbar_arrive(&done[s_]);
     }
   } else {
     // ------------------------------------------------------------ reducer
@@ -216,11 +271,12 @@ __global__ void __launch_bounds__(512) qmv_stream_kernel(const __nv_bfloat16* __
       const int r0 = r_begin + c * R;
       const int nr = min(R, r_end - r0);
       const float* red = reinterpret_cast<const float*>(stage(s) + (size_t)R * K / 2 + (size_t)R * K / 16);
-      if (lane < R * MC) {
-        const int r = lane / MC, m = lane % MC;
+      for (int v = lane; v < R * MC; v += 32) {
+        const int r = v / MC, m = v % MC;
+        const int team = r / RT, idx = (r % RT) * MC + m;
         if (r < nr && m < mc) {
           float acc = 0.0f;
-          for (int p = 0; p < P; ++p) acc += red[p * 32 + lane];
+          for (int p = 0; p < P; ++p) acc += red[(team * P + p) * 32 + idx];
           y[(size_t)(m0 + m) * N + r0 + r] = __float2bfloat16_rn(acc);
         }
       }
@@ -231,30 +287,27 @@ __global__ void __launch_bounds__(512) qmv_stream_kernel(const __nv_bfloat16* __
   __syncthreads();
 }
 
-template <int MC, int R>
-static int launch_stream(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N,
-                         int K, cudaStream_t stream, int* status) {
-  auto kern = qmv_stream_kernel<MC, R>;
+template <int MC, int RT, bool FULLK, int S>
+static int launch_stream(int T, const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M,
+                         int N, int K, cudaStream_t stream, int* status) {
+  auto kern = qmv_stream_kernel<MC, RT, FULLK, S>;
   const int P = (K + 1023) / 1024;
-  const int threads = (P + 2) * 32;
-  const size_t smem = kStreamStages * stream_stage_bytes(R, K, P) + 3 * kStreamStages * sizeof(uint64_t) + 16;
-  static int occ_cache[64] = {};     // indexed by P; idempotent, so a race only repeats the query
-  static bool attr_set[64] = {};     // per device
+  const int threads = (T * P + 2) * 32;
+  const int R = T * RT;
+  const size_t stage = stream_stage_bytes(R, K);
+  const size_t smem = S * stage + 3 * S * sizeof(uint64_t) + 16;
+  static bool attr_set[64] = {};  // per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmemBudget) !=
+        cudaSuccess)
       return fail(QVX_ERR_CUDA, "qvx_qmv: cannot raise the shared-memory limit");
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  int occ = P < 64 ? occ_cache[P] : 0;
-  if (occ == 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem) != cudaSuccess || occ < 1)
-      return fail(QVX_ERR_UNSUPPORTED, "qvx_qmv: streaming kernel does not fit (K=%d)", K);
-    if (P < 64) occ_cache[P] = occ;
-  }
   const int chunks = (M + MC - 1) / MC;
-  long long ctas = (long long)occ * num_sms() / chunks;
+  // one CTA per SM: the other half of the SM is left to the next launch
+  long long ctas = num_sms() / chunks;
   const long long need = (N + R - 1) / R;
   if (ctas > need) ctas = need;
   if (ctas < 1) ctas = 1;
@@ -270,7 +323,7 @@ static int launch_stream(const void* x, const uint32_t* w, const void* s, const 
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const __nv_bfloat16*>(x), w,
                                      static_cast<const uint16_t*>(s), static_cast<const uint16_t*>(b),
-                                     static_cast<__nv_bfloat16*>(y), M, N, K, status);
+                                     static_cast<__nv_bfloat16*>(y), M, N, K, T, status);
   if (e != cudaSuccess) return fail(QVX_ERR_CUDA, "qvx_qmv launch: %s", cudaGetErrorString(e));
   return QVX_OK;
 }
@@ -279,26 +332,34 @@ static int launch_stream(const void* x, const uint32_t* w, const void* s, const 
 // (the caller then uses the general kernel).
 int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
                    cudaStream_t stream) {
-  // at most 14 compute warps + 2 (512 threads, so up to 128 registers a thread)
-  if (K % 512 != 0 || K > 14 * 1024 || !aligned(s, 16) || !aligned(b, 16)) return -1;
+  if (K % 512 != 0 || K > kStreamMaxComputeWarps * 1024 || !aligned(s, 16) || !aligned(b, 16)) return -1;
   int* status = device_status_ptr();
   if (!status) return fail(QVX_ERR_CUDA, "qvx_qmv: device status word unavailable");
-  // rows per stage: about 16 KB of codes
-  const int R = K <= 4096 ? 8 : K <= 8192 ? 4 : K <= 16384 ? 2 : 1;
-  if (M == 1) {
-    switch (R) {
-      case 8: return launch_stream<1, 8>(x, w, s, b, y, M, N, K, stream, status);
-      case 4: return launch_stream<1, 4>(x, w, s, b, y, M, N, K, stream, status);
-      case 2: return launch_stream<1, 2>(x, w, s, b, y, M, N, K, stream, status);
-      default: return launch_stream<1, 1>(x, w, s, b, y, M, N, K, stream, status);
-    }
+  const int P = (K + 1023) / 1024;
+  const int T = P >= 8 ? 1 : 8 / P;  // about 8 compute warps
+  // rows per team per stage: the most (4, 2 or 1) that keeps a stage's codes within 16 KB
+  int rt = 4;
+  while (rt > 1 && (size_t)T * rt * K / 2 > kStreamStageCodeBytes) rt /= 2;
+  const int mc = M == 1 ? 1 : 2;  // x costs 24 registers per token
+  const bool fullk = K % 1024 == 0;
+  // ring depth: 4 stages of ~16 KB, or 6 when the stages are smaller (both fit the budget)
+  const bool deep = 6 * (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)) + 16 <= kStreamSmemBudget;
+#define QVX_STREAM_CASE(MC_, RT_)                                                                             \
+  if (mc == MC_ && rt == RT_) {                                                                               \
+    if (deep)                                                                                                 \
+      return fullk ? launch_stream<MC_, RT_, true, 6>(T, x, w, s, b, y, M, N, K, stream, status)              \
+                   : launch_stream<MC_, RT_, false, 6>(T, x, w, s, b, y, M, N, K, stream, status);            \
+    return fullk ? launch_stream<MC_, RT_, true, 4>(T, x, w, s, b, y, M, N, K, stream, status)                \
+                 : launch_stream<MC_, RT_, false, 4>(T, x, w, s, b, y, M, N, K, stream, status);              \
   }
-  switch (R) {
-    case 8: return launch_stream<2, 8>(x, w, s, b, y, M, N, K, stream, status);
-    case 4: return launch_stream<2, 4>(x, w, s, b, y, M, N, K, stream, status);
-    case 2: return launch_stream<2, 2>(x, w, s, b, y, M, N, K, stream, status);
-    default: return launch_stream<2, 1>(x, w, s, b, y, M, N, K, stream, status);
-  }
+  QVX_STREAM_CASE(1, 4)
+  QVX_STREAM_CASE(1, 2)
+  QVX_STREAM_CASE(1, 1)
+  QVX_STREAM_CASE(2, 4)
+  QVX_STREAM_CASE(2, 2)
+  QVX_STREAM_CASE(2, 1)
+#undef QVX_STREAM_CASE
+  return fail(QVX_ERR_UNSUPPORTED, "qvx_qmv: no streaming plan for M=%d K=%d", M, K);
 }
 
 }  // namespace qvx
