@@ -20,14 +20,15 @@
 // Arithmetic: exact integer dot products.  Instruction rates measured on B200 put LOP3,
 // SHF and DP4A at half rate on separate pipes, with DP4A-based unpacking sustaining ~75
 // codes/clk/SM against ~43 for mixed fp16 FMA and ~25 for fp32 bit tricks.  So:
-//   * a lane's 32 inputs of one token become 24-bit fixed point against the slice max
-//     (x_fix = rint(x * 2^(23-E)), 2^(E-1) <= max|x| < 2^E, exact for every bf16 value
-//     within 2^15 of the max), split into byte planes p0, p1 (unsigned) and p2 (signed),
-//     packed four inputs per register in the order the codes unpack;
+//   * a lane's 32 inputs of one token become 22-bit fixed point against the slice max
+//     (x_fix = rint(x * 2^(22-E)), 2^(E-1) <= max|x| < 2^E, exact for every bf16 value
+//     within a factor 2^14 of the max, error <= 2^-23 max|x| otherwise), split into byte
+//     planes p0, p1 (unsigned) and p2 (signed), packed four inputs per register in the
+//     order the codes unpack;
 //   * a packed word w gives its even codes as bytes with one LOP3 (w & 0x0F0F0F0F) and its
 //     odd codes with a shift and a LOP3; three DP4As per 4 codes accumulate
 //     sum q * p_j in int32 (no overflow: 15*255*32 < 2^17);
-//   * per row: Q = a0 + 256 a1 + 65536 a2, sum(q x) = 2^(E-23) Q, and the group term of the
+//   * per row: Q = a0 + 256 a1 + 65536 a2, sum(q x) = 2^(E-22) Q, and the group term of the
 //     reference factorisation s*sum(q x) + b*sum(x) (engine/kernels.py:151-171).
 #include "sm100.cuh"
 
@@ -100,8 +101,8 @@ __device__ __forceinline__ void make_planes(const float (&xf)[32], XPlanes& xp) 
   int E = 0;
   if (mx > 0.0f && isfinite(mx)) frexpf(mx, &E);  // 2^(E-1) <= mx < 2^E
   E = max(E, -100);
-  const float up = ldexpf(1.0f, 23 - E);
-  xp.scale = ldexpf(1.0f, E - 23);
+  const float up = ldexpf(1.0f, 22 - E);
+  xp.scale = ldexpf(1.0f, E - 22);
   xp.xsum = sum;
 #pragma unroll
   for (int w = 0; w < 4; ++w)
@@ -110,7 +111,9 @@ __device__ __forceinline__ void make_planes(const float (&xf)[32], XPlanes& xp) 
       uint32_t b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int v = __float2int_rn(xf[8 * w + h + 2 * i] * up);  // |v| < 2^23
+        // x * 2^(22-E) has |.| < 2^22, so adding 1.5 * 2^23 lands in [2^23, 2^24) where the
+        // float spacing is 1: one FFMA rounds to the nearest integer, exactly
+        const int v = __float_as_int(fmaf(xf[8 * w + h + 2 * i], up, 12582912.0f)) - 0x4B400000;
         b0 |= ((uint32_t)v & 0xFFu) << (8 * i);
         b1 |= (((uint32_t)v >> 8) & 0xFFu) << (8 * i);
         b2 |= (((uint32_t)v >> 16) & 0xFFu) << (8 * i);
