@@ -49,9 +49,130 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=32, help="decoder layers (32 = the full 9B shape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the M=2/4/8 side measurements")
-    ap.add_argument("--profile", action="store_true",
-                    help="small run for profilers: no graph, no clocks, no CPU baseline")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the config-2/3 kernel measurements (prefill qmm, quantize, gated DeltaNet)")
+    ap.add_argument("--profile", nargs="?", const="step", default=None,
+                    choices=["step", "qmm", "qmm_small", "quantize", "gd_prefill", "gd_decode"],
+                    help="run one case eagerly for a profiler (no graph, clocks or CPU baseline)")
     return ap.parse_args()
+
+
+# ------------------------------------------------------------------ config 2 / 3 kernels
+
+def _cuda_time(torch, fn, reps, warm=3):
+    """Device time per call (ms) of `fn` replayed from a CUDA graph of `reps` calls, so host
+    overhead of the Python wrapper is not counted."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) / reps  # ms
+
+
+def config_cases(torch, device, small=False):
+    """Inputs of BASELINE configs 2 (quantize + prefill qmm) and 3 (gated DeltaNet)."""
+    import qvex
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    N, K, M = (4096, 4096, 512) if small else (12288, 4096, 2048)
+    W = (torch.randn((N, K), device=device, generator=g) * 0.02).to(torch.bfloat16)
+    wq, s, b = qvex.quantize(W)
+    x = torch.randn((M, K), device=device, generator=g).to(torch.bfloat16)
+    return {"W": W, "wq": wq, "s": s, "b": b, "x": x, "M": M, "N": N, "K": K}
+
+
+def gd_case(torch, device, B, T):
+    """Config 3: Hk=16, Hv=32, D=128; q, k L2-normalised, v ~ N(0,1), a, b ~ N(0,1),
+    A_log = dt_bias = 0 (log-decay = -softplus(a), beta = sigmoid(b)), state N(0,1)*0.1."""
+    g = torch.Generator(device=device)
+    g.manual_seed(3)
+    Hk, Hv, D = 16, 32, 128
+    q = torch.nn.functional.normalize(torch.randn((B, T, Hk, D), device=device, generator=g), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn((B, T, Hk, D), device=device, generator=g), dim=-1)
+    v = torch.randn((B, T, Hv, D), device=device, generator=g)
+    a = torch.randn((B, T, Hv), device=device, generator=g)
+    bb = torch.randn((B, T, Hv), device=device, generator=g)
+    st = torch.randn((B, Hv, D, D), device=device, generator=g) * 0.1
+    z = torch.zeros(Hv, device=device)
+    bf = torch.bfloat16
+    return (q.to(bf), k.to(bf), v.to(bf), a.to(bf), bb.to(bf), z, z, st.float())
+
+
+def measure_configs(torch, device, hbm_peak, tc_peak):
+    """Device-timed throughput of the config-2 and config-3 kernels with their rooflines."""
+    import qvex
+    out = {}
+    c = config_cases(torch, device)
+    M, N, K = c["M"], c["N"], c["K"]
+    # quantize / pack: reads bf16 W, writes codes + scales + biases; two copies of W
+    # alternate so that 200 MB of inputs (> 126 MB L2) are streamed
+    qb = N * K * 2 + N * K // 2 + N * (K // 64) * 4
+    Ws = [c["W"], c["W"].clone()]
+    it = iter(range(1 << 30))
+    ms = _cuda_time(torch, lambda: qvex.quantize(Ws[next(it) & 1]), 20)
+    del Ws
+    out["quantize_config2"] = {"ms": round(ms, 4), "gbs": round(qb / ms / 1e6, 1),
+                               "frac_hbm": round(qb / ms / 1e6 / hbm_peak, 3), "bytes": qb}
+    # prefill qmm (tcgen05): 2 M N K flops, prepasses included
+    ws = torch.empty(qvex.qmm_workspace_size(M, N, K), dtype=torch.uint8, device=device)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=device)
+    ms = _cuda_time(torch, lambda: qvex.quantized_matmul(c["x"], c["wq"], c["s"], c["b"], out=y, workspace=ws), 20)
+    fl = 2.0 * M * N * K
+    out["qmm_config2"] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
+                          "frac_bf16_dense": round(fl / ms / 1e9 / tc_peak, 3), "M": M, "N": N, "K": K}
+    del c, ws, y
+    # gated DeltaNet: decode step (HBM: state in + out) and 2048-step prefill (serial in T)
+    for B, T in ((1, 1), (8, 1), (1, 2048), (8, 2048)):
+        args = gd_case(torch, device, B, T)
+        # decode steps rotate over enough distinct states (>= 256 MB) that they come from HBM
+        n_st = max(1, (256 << 20) // (B * 32 * 128 * 128 * 4)) if T == 1 else 1
+        states = [args[-1]] + [args[-1].clone() for _ in range(n_st - 1)]
+        outs = [torch.empty_like(args[-1]) for _ in range(n_st)]
+        it = iter(range(1 << 30))
+
+        def call():
+            i = next(it) % n_st
+            return qvex.gated_delta(*args[:-1], states[i], out_state=outs[i])
+        ms = _cuda_time(torch, call, 10 if T > 1 else 2 * n_st)
+        del states, outs
+        state_bytes = B * 32 * 128 * 128 * 4 * 2
+        io_bytes = B * T * (2 * 16 * 128 + 2 * 32 * 128 + 2 * 32) * 2
+        flops = 7.0 * 128 * 128 * 32 * B * T
+        out[f"gated_delta_B{B}_T{T}"] = {"ms": round(ms, 4), "steps_per_s": round(T / ms * 1e3, 1),
+                                        "gbs": round((state_bytes + io_bytes) / ms / 1e6, 1),
+                                        "fp32_tflops": round(flops / ms / 1e9, 3)}
+    return out
+
+
+def profile_case(torch, device, case, reps):
+    """One eagerly-launched case for ncu (small enough for a full-section capture)."""
+    import qvex
+    if case in ("qmm", "qmm_small"):
+        c = config_cases(torch, device, small=(case == "qmm_small"))
+        for _ in range(reps):
+            qvex.quantized_matmul(c["x"], c["wq"], c["s"], c["b"])
+    elif case == "quantize":
+        c = config_cases(torch, device)
+        for _ in range(reps):
+            qvex.quantize(c["W"])
+    else:
+        B, T = (8, 2048) if case == "gd_prefill" else (8, 1)
+        args = gd_case(torch, device, B, T)
+        for _ in range(reps):
+            qvex.gated_delta(*args)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_run": case, "reps": reps}))
 
 
 # ------------------------------------------------------------------ environment
@@ -62,6 +183,14 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def tc_peak() -> float:
+    """Dense bf16 tensor peak (TFLOP/s): measured burst figure, else the fallback."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
 
 
 def host_threads() -> int:
@@ -172,6 +301,10 @@ def run_ours(args):
 
     import qvex
     qvex.load_library()
+
+    if args.profile and args.profile != "step":
+        profile_case(torch, device, args.profile, max(args.warmup, 1))
+        return
 
     shape = Qwen35Shape(layers=args.layers)
     M = args.m
@@ -316,6 +449,10 @@ def run_ours(args):
             extra[f"M={m2}"] = round(bm / (ms_m / max(args.steps // 4, 10) * 1e-3) / 1e9, 1)
             del gm
 
+    configs = None
+    if world == 1 and not args.no_configs:
+        configs = measure_configs(torch, device, peak, tc_peak())
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(torch, lins, xs, M, budget_s=3.0)
@@ -335,7 +472,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic_per_launch(bytes_rank / launches_per_step),
-                         "kernel": "qmv_kernel<1,32,4> (all launches of the step)"},
+                         "kernel": "qmv_stream_kernel (all 145 launches of the step, gaps included)"},
             "lm_head_qmv": {"gbs": round(lm_gbs, 1), "ms": round(lm_ms, 4), "frac": round(lm_gbs / peak, 4)},
             "qmv_gbs_by_m": extra,
             "e2e": {"value": round(e2e_val, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -344,6 +481,8 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if configs:
+            rec["configs"] = configs
         if cpu:
             rec["cpu_baseline"] = cpu
         print(json.dumps(rec))
