@@ -15,7 +15,8 @@
 //                                        dequantiser produces pairs in)
 //   [off_exp]      e     int32 [M]
 //   [off_fexp]     f     int32 [N]     per weight row exponent
-//   [off_prm]      prm   uint2 [K/64, N padded to 256] group-major fp16 multipliers (S24, S20 | B)
+//   [off_prm]      prm   uint2 [G/2, N padded to 256, 2] fp16 multipliers (S24, S20 | B) of
+//                                        groups (2j, 2j+1), G = K/64 rounded up to even
 #include "common.cuh"
 
 namespace qvx {
@@ -24,6 +25,7 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
                   __nv_bfloat16* y, int M, int N, int K, cudaStream_t stream);
 int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm, int N, int K, cudaStream_t stream);
 int qmm_row_pad(int N);
+size_t qmm_prm_bytes(int N, int K);
 int qmv_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
                 int K, cudaStream_t stream);
 int check_qparams(const char* who, const void* x, const uint32_t* w, const void* s, const void* b, const void* y,
@@ -41,7 +43,7 @@ static QmmWorkspace qmm_ws_layout(int M, int N, int K) {
   l.off_exp = align256((size_t)M * K * sizeof(__half));
   l.off_fexp = l.off_exp + align256((size_t)M * sizeof(int32_t));
   l.off_prm = l.off_fexp + align256((size_t)N * sizeof(int32_t));
-  l.total = l.off_prm + align256((size_t)qmm_row_pad(N) * (K / 64) * sizeof(uint2));
+  l.total = l.off_prm + align256(qmm_prm_bytes(N, K));
   return l;
 }
 

@@ -6,22 +6,32 @@
 //   B = x, fp16 (prepass in qmm.cu), staged by TMA into 128-byte-swizzled shared memory;
 //   D = fp32 accumulators in tensor memory, read back by tcgen05.ld in the epilogue.
 //
-// Tile: 256 weight rows (two M=128 MMAs into two accumulators) x 128 tokens (MMA N) x
-// K-steps of 64 (one quantisation group).  One CTA per SM, persistent over tiles; tile
+// Tile: 256 weight rows (two M=128 MMAs into two accumulators) x 128 tokens (MMA N).
+// One pipeline stage covers K = 128 (two quantisation groups): 16 MMAs of K=16, about
+// 1100 SM cycles of tensor work.  Every mbarrier operation costs one thread ~120 cycles
+// and a thread's operations run back to back, so a stage must carry enough MMA work to
+// hide its handshakes: with K = 64 per stage the producer and MMA threads alone took
+// longer per stage than the tensor cores.  One CTA per SM, persistent over tiles; tile
 // t -> (weight block t / tiles_m, token block t % tiles_m), so CTAs running at the same
 // time share weight rows in L2 while x stays L2-resident.
 //
+// One ring of S stages, each holding the stage's x tile (2 x 16 KB), code tile (16 KB)
+// and group multipliers (4 KB), filled by TMA (full[s]) and released by ONE tcgen05
+// commit of the MMA thread (empty[s]) -- the dequantisers have read the codes before the
+// MMAs that release the stage could start.  The dequantised A tile has two tensor-memory
+// stages; step L writes stage L % 2, which is free once the MMAs of step L - 2 are done,
+// i.e. once empty[(L - 2) % S] has completed that step's phase: no separate barrier.
+//
 // Warp roles (22 warps):
-//   0..15  dequant: two groups of 8 warps take alternate K steps (two steps in flight);
+//   0..15  dequant: two groups of 8 warps take alternate steps (group g owns A stage g);
 //          within a group warp w owns TMEM lanes 32*(w%4).. of weight-row half (w/4)%2,
-//          one weight row per thread, and writes its 64 fp16 values (32 columns).
-//   16..19 epilogue: tcgen05.ld of both accumulators, scale by 2^(f_n + e_m), bf16 stores.
-//   20     TMA producer: per K step the x tile (2-D TMA, swizzled), the 256x32-byte code
-//          tile (2-D TMA) and the step's 256 group multipliers (2 KB bulk copy).  Loading
-//          codes per thread instead (cp.async of each row's 32 bytes) issues 32 L1
-//          wavefronts per warp instruction and was measured to cap the kernel at ~0.8 us
-//          per K step with every other stage removed.
-//   21     MMA issuer (one thread): 2 x 4 tcgen05.mma per K step, commits free the stages.
+//          one weight row per thread, and writes its 128 fp16 values (64 columns).
+//   16..19 epilogue: tcgen05.ld of both accumulators, scale by 2^(f_n + e_m), bf16 into a
+//          shared-memory tile written out by one TMA store (direct stores when y's rows
+//          are not 16-byte multiples).  The accumulator goes back to the MMA issuer as soon
+//          as its last chunk is in registers.
+//   20     TMA producer (one thread).
+//   21     MMA issuer (one thread): 2 x 8 tcgen05.mma per step, one commit per step.
 //
 // Dequantisation with one HFMA2 per two weights.  A nibble masked in place is already an
 // fp16 subnormal: (w & 0x000F000F) is the half2 (q0, q4) * 2^-24 and (w & 0x00F000F0) is
@@ -31,6 +41,12 @@
 // fp16((q s + b) * 2^-f) with a single rounding -- the same value as an fp32 dequant
 // rounded to fp16.  The pairs come out as (k, k+4) within each 8 inputs, so the x
 // prepass stores x in that order: the contraction is unchanged because A and B share it.
+//
+// K that is not a multiple of 128 (an odd number of groups) runs a last half-empty stage:
+// TMA fills the x and code columns past K with zeros and the prepass pads the multipliers
+// of the missing group with zeros, so it contributes exactly 0.
+#include <cstring>
+
 #include "sm100.cuh"
 
 namespace qvx {
@@ -38,10 +54,8 @@ namespace tc {
 
 constexpr int BM = 256;  // weight rows per tile
 constexpr int BN = 128;  // tokens per tile (MMA N)
-constexpr int BK = 64;   // K per step (one group)
-constexpr int SA = 4;    // A stages (tensor memory)
-constexpr int SB = 6;    // x stages (shared memory)
-constexpr int SC = 8;    // code + multiplier stages (shared memory); even, so groups keep parity
+constexpr int BK = 128;  // K per stage (two groups)
+constexpr int S = 3;     // ring stages (shared memory)
 constexpr int DQ_GROUPS = 2;
 constexpr int DQ_WARPS_PER_GROUP = 8;  // 2 halves x 4 lane quarters
 constexpr int NUM_DQ_WARPS = DQ_GROUPS * DQ_WARPS_PER_GROUP;
@@ -49,21 +63,26 @@ constexpr int EPI_WARP0 = 16;
 constexpr int WARP_TMA = 20;
 constexpr int WARP_MMA = 21;
 constexpr int THREADS = 22 * 32;
+static_assert(WARP_MMA == WARP_TMA + 1 && THREADS == (WARP_MMA + 1) * 32, "the MMA warp is the last warp");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t A_COL0 = 256;  // A stage s, half h: columns A_COL0 + (2s + h) * 32
-constexpr uint32_t B_STAGE_BYTES = BN * BK * 2;           // 16 KB of x
-constexpr uint32_t C_CODE_BYTES = BM * (BK / 8) * 4;      // 8 KB of codes: [256 rows][8 words]
-constexpr uint32_t C_PRM_BYTES = BM * 8;                  // 2 KB of multipliers: [256 rows] x uint2
-constexpr uint32_t C_STAGE_BYTES = C_CODE_BYTES + C_PRM_BYTES;
+constexpr uint32_t A_COL0 = 256;  // A stage a, half h: columns A_COL0 + (2a + h) * 64
+constexpr uint32_t X_HALF_BYTES = BN * 64 * 2;             // 16 KB: 128 tokens x 64 k, one swizzle span wide
+constexpr uint32_t X_BYTES = 2 * X_HALF_BYTES;              // 32 KB
+constexpr uint32_t CODE_BYTES = BM * (BK / 8) * 4;          // 16 KB: [256 rows][16 words], 64-byte swizzle
+constexpr uint32_t PRM_BYTES = BM * 2 * 8;                  // 4 KB: [256 rows][2 groups] x uint2
+constexpr uint32_t STAGE_BYTES = X_BYTES + CODE_BYTES + PRM_BYTES;
+static_assert(STAGE_BYTES % 1024 == 0, "stages keep 1024-byte alignment (swizzle atoms)");
 
 // shared memory layout (offsets from a 1024-byte aligned base)
-constexpr uint32_t OFF_B = 0;
-constexpr uint32_t OFF_C = OFF_B + SB * B_STAGE_BYTES;
-constexpr uint32_t OFF_BAR = OFF_C + SC * C_STAGE_BYTES;
-constexpr uint32_t NUM_BARS = 2 * SB + 2 * SC + 2 * SA + 3;
+constexpr uint32_t OFF_CODE = X_BYTES;
+constexpr uint32_t OFF_PRM = X_BYTES + CODE_BYTES;
+constexpr uint32_t OFF_EPI = S * STAGE_BYTES;  // bf16 output tile [BN][BM] for the TMA store
+constexpr uint32_t EPI_BYTES = BN * BM * 2;    // 64 KB
+constexpr uint32_t OFF_BAR = OFF_EPI + EPI_BYTES;
+constexpr uint32_t NUM_BARS = 2 * S + DQ_GROUPS + 5;
 constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-static_assert(SC % DQ_GROUPS == 0 && SA % DQ_GROUPS == 0, "stages must split evenly between dequant groups");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 
 // instruction descriptor: D f32, A f16, B f16, both K-major, N = 128, M = 128
 constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
@@ -74,53 +93,71 @@ __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c
   return d;
 }
 
-__device__ __forceinline__ float exp2i(int e) {
-  return (e >= -126 && e <= 127) ? __int_as_float((e + 127) << 23) : ldexpf(1.0f, e);
+// 2^k for k clamped to the normal range
+__device__ __forceinline__ float pow2_normal(int k) { return __int_as_float((min(max(k, -126), 127) + 127) << 23); }
+
+// v * 2^e for any |e| <= 252 as two exact power-of-two multiplies (the first is exact
+// unless the intermediate leaves the float range)
+__device__ __forceinline__ float scale_pow2(float v, int e) {
+  const int e1 = e / 2;
+  return (v * pow2_normal(e1)) * pow2_normal(e - e1);
 }
 
+// 8 code words of one group -> 32 half2 words (pairs (k, k+4)) with multipliers (s24|s20, b)
+__device__ __forceinline__ void dequant_group(const uint4& c0, const uint4& c1, uint32_t pmx, uint32_t pmy,
+                                              uint32_t (&v)[32]) {
+  const uint32_t s24 = __byte_perm(pmx, pmx, 0x1010), s20 = __byte_perm(pmx, pmx, 0x3232);
+  const uint32_t bb = __byte_perm(pmy, pmy, 0x1010);
+  const uint32_t wd[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t ww = wd[q], w8 = wd[q] >> 8;
+    v[4 * q + 0] = hfma2_u32(ww & 0x000F000Fu, s24, bb);  // (q0, q4)
+    v[4 * q + 1] = hfma2_u32(ww & 0x00F000F0u, s20, bb);  // (q1, q5)
+    v[4 * q + 2] = hfma2_u32(w8 & 0x000F000Fu, s24, bb);  // (q2, q6)
+    v[4 * q + 3] = hfma2_u32(w8 & 0x00F000F0u, s20, bb);  // (q3, q7)
+  }
+}
+
+template <bool kStaged>
 __global__ void __launch_bounds__(THREADS, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                  const uint2* __restrict__ prm, const int32_t* __restrict__ fexp, const int32_t* __restrict__ xexp,
-                  __nv_bfloat16* __restrict__ y, int M, int N, int K, int n_pad, int* status) {
+                  const __grid_constant__ CUtensorMap tmap_y, const uint2* __restrict__ prm,
+                  const int32_t* __restrict__ fexp, const int32_t* __restrict__ xexp, __nv_bfloat16* __restrict__ y,
+                  int M, int N, int K, int n_pad, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* full_b = bars;
-  uint64_t* empty_b = full_b + SB;
-  uint64_t* full_c = empty_b + SB;
-  uint64_t* empty_c = full_c + SC;
-  uint64_t* full_a = empty_c + SC;
-  uint64_t* empty_a = full_a + SA;
-  uint64_t* acc_full = empty_a + SA;
+  uint64_t* full = bars;
+  uint64_t* empty = full + S;
+  uint64_t* full_a = empty + S;
+  uint64_t* acc_full = full_a + DQ_GROUPS;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
+  uint64_t* epi_full = drain + 1;
+  uint64_t* epi_free = epi_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkb = K / BK;
+  const int nks = (K + BK - 1) / BK;  // stages per tile
   const int tiles_m = (M + BN - 1) / BN;
   const int tiles_n = (N + BM - 1) / BM;
   const int ntiles = tiles_m * tiles_n;
   const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int total = my_tiles * nkb;  // K steps this CTA runs
+  const int total = my_tiles * nks;  // stages this CTA runs
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SB; ++i) {
-      mbar_init(&full_b[i], 1);
-      mbar_init(&empty_b[i], 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < SC; ++i) {
-      mbar_init(&full_c[i], 1);
-      mbar_init(&empty_c[i], DQ_WARPS_PER_GROUP);
-    }
-    for (int i = 0; i < SA; ++i) {
-      mbar_init(&full_a[i], DQ_WARPS_PER_GROUP);
-      mbar_init(&empty_a[i], 1);
-    }
+    for (int i = 0; i < DQ_GROUPS; ++i) mbar_init(&full_a[i], DQ_WARPS_PER_GROUP);
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
     mbar_init(drain, 1);
+    mbar_init(epi_full, 4);
+    mbar_init(epi_free, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -136,51 +173,54 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp < NUM_DQ_WARPS) {
     // ------------------------------------------------------------ dequant
     const int quarter = warp & 3, half = (warp >> 2) & 1, group = warp >> 3;
-    const int row_in_tile = half * 128 + quarter * 32 + lane;
+    const int r = half * 128 + quarter * 32 + lane;  // weight row within the tile
+    const uint32_t swz = (uint32_t)((r >> 1) & 3);   // 64-byte swizzle of the code tile
+    const uint32_t a_col = tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)(group * 2 + half) * 64;
     bool ok = true;
     for (int L = group; L < total && ok; L += DQ_GROUPS) {
-      const int sc = L % SC;
-      if (!(ok = mbar_wait(&full_c[sc], (uint32_t)(L / SC) & 1u, abort_flag, status))) break;
-      const uint8_t* cst = smem + OFF_C + sc * C_STAGE_BYTES;
-      const uint4 c0 = *reinterpret_cast<const uint4*>(cst + row_in_tile * 32);
-      const uint4 c1 = *reinterpret_cast<const uint4*>(cst + row_in_tile * 32 + 16);
-      const uint2 pm = *reinterpret_cast<const uint2*>(cst + C_CODE_BYTES + row_in_tile * 8);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_c[sc]);  // the stage's data is in registers now
-      const uint32_t s24 = __byte_perm(pm.x, pm.x, 0x1010), s20 = __byte_perm(pm.x, pm.x, 0x3232);
-      const uint32_t bb = __byte_perm(pm.y, pm.y, 0x1010);
-      const uint32_t wd[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      uint32_t v[32];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint32_t ww = wd[q], w8 = wd[q] >> 8;
-        v[4 * q + 0] = hfma2_u32(ww & 0x000F000Fu, s24, bb);  // (q0, q4)
-        v[4 * q + 1] = hfma2_u32(ww & 0x00F000F0u, s20, bb);  // (q1, q5)
-        v[4 * q + 2] = hfma2_u32(w8 & 0x000F000Fu, s24, bb);  // (q2, q6)
-        v[4 * q + 3] = hfma2_u32(w8 & 0x00F000F0u, s20, bb);  // (q3, q7)
+      const int s = L % S;
+      if (!(ok = mbar_wait(&full[s], (uint32_t)(L / S) & 1u, abort_flag, status))) break;
+      const uint8_t* st = smem + s * STAGE_BYTES;
+      const uint8_t* crow = st + OFF_CODE + r * 64;
+      const uint4 c0 = *reinterpret_cast<const uint4*>(crow + ((0u ^ swz) << 4));
+      const uint4 c1 = *reinterpret_cast<const uint4*>(crow + ((1u ^ swz) << 4));
+      const uint4 c2 = *reinterpret_cast<const uint4*>(crow + ((2u ^ swz) << 4));
+      const uint4 c3 = *reinterpret_cast<const uint4*>(crow + ((3u ^ swz) << 4));
+      const uint4 pm = *reinterpret_cast<const uint4*>(st + OFF_PRM + r * 16);
+      // A stage `group` is free once the MMAs of step L - 2 have completed
+      if (L >= DQ_GROUPS) {
+        const int Lp = L - DQ_GROUPS;
+        if (!(ok = mbar_wait(&empty[Lp % S], (uint32_t)(Lp / S) & 1u, abort_flag, status))) break;
       }
-      const int sa = L % SA;
-      if (!(ok = mbar_wait(&empty_a[sa], ((uint32_t)(L / SA) & 1u) ^ 1u, abort_flag, status))) break;
+      __syncwarp();  // tcgen05.st is warp-aligned; the lanes left their polls independently
       tc_fence_after();
-      tmem_st_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)(sa * 2 + half) * 32, v);
+      {
+        uint32_t v[32];
+        dequant_group(c0, c1, pm.x, pm.y, v);
+        tmem_st_32x32b_x32(a_col, v);
+      }
+      {
+        uint32_t v[32];
+        dequant_group(c2, c3, pm.z, pm.w, v);
+        tmem_st_32x32b_x32(a_col + 32, v);
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[sa]);
+      if (lane == 0) mbar_arrive(&full_a[group]);
     }
   } else if (warp < EPI_WARP0 + 4) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
+    const bool storer = (warp == EPI_WARP0 && lane == 0);  // issues the tile's TMA store
+    uint16_t* stage_y = reinterpret_cast<uint16_t*>(smem + OFF_EPI);  // [BN tokens][BM rows] bf16
     for (int lt = 0; lt < my_tiles; ++lt) {
       const int t = (int)blockIdx.x + lt * (int)gridDim.x;
       const int n_base = (t / tiles_m) * BM, m_base = (t % tiles_m) * BN;
       // exponents do not depend on the MMA: fetch them before waiting for the accumulator
-      int fn[2], e_lane[BN / 32];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = n_base + h * 128 + quarter * 32 + lane;
-        fn[h] = n < N ? fexp[n] : 0;
-      }
+      const int n0 = n_base + quarter * 32 + lane, n1 = n0 + 128;
+      const int fn0 = n0 < N ? fexp[n0] : 0, fn1 = n1 < N ? fexp[n1] : 0;
+      int e_lane[BN / 32];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         const int mcol = m_base + c * 32 + lane;
@@ -188,76 +228,125 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!mbar_wait(acc_full, (uint32_t)lt & 1u, abort_flag, status)) break;
       tc_fence_after();
+      if (kStaged && lt > 0) {
+        // the previous tile's store must have read the staging tile before it is rewritten
+        if (storer) {
+          bulk_wait_read_all();
+          mbar_arrive(epi_free);
+        }
+        if (!mbar_wait(epi_free, (uint32_t)(lt - 1) & 1u, abort_flag, status)) break;
+      }
+      __syncwarp();  // tcgen05.ld is warp-aligned
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
-        const int n = n_base + h * 128 + quarter * 32 + lane;
+        const int nr = h * 128 + quarter * 32 + lane;  // row within the tile
+        const int n = n_base + nr;
+        // a select, not fn[h]: a runtime-indexed array would live in local memory
+        const int fnh = h ? fn1 : fn0;
+        // one warp-uniform test per 32 x 32 block: 2^(f_n + e_m) built from bits when in range
+        const int fmin = __reduce_min_sync(0xffffffffu, fnh), fmax = __reduce_max_sync(0xffffffffu, fnh);
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * 128 + c * 32), v);
           tmem_wait_ld();
+          if (h == 1 && c == BN / 32 - 1) {
+            // the whole accumulator is in registers now: hand it back to the MMA issuer
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+          }
+          const int emin = __reduce_min_sync(0xffffffffu, e_lane[c]);
+          const int emax = __reduce_max_sync(0xffffffffu, e_lane[c]);
+          const bool fast = fmin + emin >= -126 && fmax + emax <= 127;
+          auto put = [&](int j, float val) {
+            const __nv_bfloat16 o = __float2bfloat16_rn(val);
+            if (kStaged) {
+              stage_y[(c * 32 + j) * BM + nr] = __bfloat16_as_ushort(o);
+            } else {
+              const int m = m_base + c * 32 + j;
+              if (m < M && n < N) y[(size_t)m * N + n] = o;
+            }
+          };
+          if (fast) {
+            const int fb = fnh + 127;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int ej = __shfl_sync(0xffffffffu, e_lane[c], j);
-            const int m = m_base + c * 32 + j;
-            if (m < M && n < N)
-              y[(size_t)m * N + n] = __float2bfloat16_rn(__uint_as_float(v[j]) * exp2i(fn[h] + ej));
+            for (int j = 0; j < 32; ++j) {
+              const int ej = __shfl_sync(0xffffffffu, e_lane[c], j);
+              put(j, __uint_as_float(v[j]) * __int_as_float((fb + ej) << 23));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int ej = __shfl_sync(0xffffffffu, e_lane[c], j);
+              put(j, scale_pow2(__uint_as_float(v[j]), fnh + ej));
+            }
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (kStaged) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(epi_full);
+        if (storer) {
+          if (!mbar_wait(epi_full, (uint32_t)lt & 1u, abort_flag, status)) break;
+          tma_tile_2d_s2g(&tmap_y, smem_u32(stage_y), n_base, m_base);
+          bulk_commit_group();
+        }
+      }
     }
+    if (kStaged && storer) bulk_wait_all();
   } else if (warp == WARP_TMA) {
     // ------------------------------------------------------------ x, code and multiplier tiles
     if (lane == 0) {
-      int ic = 0, ib = 0;  // code / x stages issued so far
+      int it = 0;  // stages issued so far
       bool ok = true;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
         const int t = (int)blockIdx.x + lt * (int)gridDim.x;
         const int n_base = (t / tiles_m) * BM, m_base = (t % tiles_m) * BN;
-        for (int kb = 0; kb < nkb && ok; ++kb) {
-          const int sc = ic % SC;
-          if (!(ok = mbar_wait(&empty_c[sc], ((uint32_t)(ic / SC) & 1u) ^ 1u, abort_flag, status))) break;
-          uint8_t* cst = smem + OFF_C + sc * C_STAGE_BYTES;
-          mbar_arrive_expect_tx(&full_c[sc], C_CODE_BYTES + C_PRM_BYTES);
-          tma_tile_2d_g2s(smem_u32(cst), &tmap_w, &full_c[sc], kb * (BK / 8), n_base);
-          tma_bulk_g2s(cst + C_CODE_BYTES, prm + (size_t)kb * n_pad + n_base, C_PRM_BYTES, &full_c[sc]);
-          ++ic;
-          const int sb = ib % SB;
-          if (!(ok = mbar_wait(&empty_b[sb], ((uint32_t)(ib / SB) & 1u) ^ 1u, abort_flag, status))) break;
-          mbar_arrive_expect_tx(&full_b[sb], B_STAGE_BYTES);
-          tma_tile_2d_g2s(smem_u32(smem + OFF_B + sb * B_STAGE_BYTES), &tmap_x, &full_b[sb], kb * BK, m_base);
-          ++ib;
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const int s = it % S;
+          if (!(ok = mbar_wait(&empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, abort_flag, status))) break;
+          uint8_t* st = smem + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          tma_tile_2d_g2s(smem_u32(st), &tmap_x, &full[s], ks * BK, m_base);
+          tma_tile_2d_g2s(smem_u32(st + X_HALF_BYTES), &tmap_x, &full[s], ks * BK + 64, m_base);
+          tma_tile_2d_g2s(smem_u32(st + OFF_CODE), &tmap_w, &full[s], ks * (BK / 8), n_base);
+          tma_bulk_g2s(st + OFF_PRM, prm + ((size_t)ks * n_pad + n_base) * 2, PRM_BYTES, &full[s]);
         }
       }
       // let the copies already issued land before the CTA can exit
-      for (int j = max(0, ic - SC); j < ic; ++j) mbar_wait_drain(&full_c[j % SC], (uint32_t)(j / SC) & 1u, status);
-      for (int j = max(0, ib - SB); j < ib; ++j) mbar_wait_drain(&full_b[j % SB], (uint32_t)(j / SB) & 1u, status);
+      for (int j = max(0, it - S); j < it; ++j) mbar_wait_drain(&full[j % S], (uint32_t)(j / S) & 1u, status);
     }
   } else {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      // The waits for stage it + 1 sit between the MMAs of stage it and its commit: the
+      // tensor cores are still working through the queued MMAs while this thread polls,
+      // instead of idling for the ~300 cycles two barrier waits take.
+      auto wait_stage = [&](int i) {
+        return mbar_wait(&full[i % S], (uint32_t)(i / S) & 1u, abort_flag, status) &&
+               mbar_wait(&full_a[i % DQ_GROUPS], (uint32_t)(i / DQ_GROUPS) & 1u, abort_flag, status);
+      };
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
         if (!(ok = mbar_wait(acc_empty, ((uint32_t)lt & 1u) ^ 1u, abort_flag, status))) break;
-        tc_fence_after();
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int sa = it % SA, sb = it % SB;
-          if (!(ok = mbar_wait(&full_a[sa], (uint32_t)(it / SA) & 1u, abort_flag, status))) break;
-          if (!(ok = mbar_wait(&full_b[sb], (uint32_t)(it / SB) & 1u, abort_flag, status))) break;
+        if (!(ok = wait_stage(it))) break;
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const int s = it % S, a = it % DQ_GROUPS;
           tc_fence_after();
-          const uint32_t b_addr = smem_u32(smem + OFF_B + sb * B_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
           for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int j = 0; j < BK / 16; ++j)
-              tc_mma_ts_f16(tmem + (uint32_t)(h * 128), tmem + A_COL0 + (uint32_t)(sa * 2 + h) * 32 + j * 8,
-                            smem_desc_sw128(b_addr + j * 32), IDESC, (kb > 0 || j > 0) ? 1u : 0u);
-          tc_commit(&empty_a[sa]);
-          tc_commit(&empty_b[sb]);
+              tc_mma_ts_f16(tmem + (uint32_t)(h * 128), tmem + A_COL0 + (uint32_t)(a * 2 + h) * 64 + j * 8,
+                            smem_desc_sw128(b_addr + (j >> 2) * X_HALF_BYTES + (j & 3) * 32), IDESC,
+                            (ks > 0 || j > 0) ? 1u : 0u);
+          if (ks + 1 < nks) ok = wait_stage(it + 1);
+          tc_commit(&empty[s]);
+          if (!ok) break;
         }
         if (ok) tc_commit(acc_full);
       }
@@ -274,16 +363,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // Per weight row: exponent f (so the fp16 multipliers stay in range); per group the
-// multipliers (S24, S20 | B) as two half2 words, stored group-major prm[g][n] (rows padded
-// to n_pad with zeros) so that one K step of a 256-row tile is 2 KB contiguous.  One warp
-// per row.
+// multipliers (S24, S20 | B) as two half2 words, stored prm[g / 2][n][g % 2] (rows padded
+// to n_pad and the group count to even, with zeros) so that one stage of a 256-row tile
+// is 4 KB contiguous and one row's two groups are one 16-byte load.  One warp per row.
 __global__ void __launch_bounds__(256) w_prep_kernel(const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi,
                                                      int32_t* __restrict__ fexp, uint2* __restrict__ prm, int N,
                                                      int n_pad, int G) {
   const int n = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (n >= n_pad) return;
+  const int Gp = (G + 1) & ~1;
+  auto at = [&](int g) -> uint2& { return prm[((size_t)(g >> 1) * n_pad + n) * 2 + (g & 1)]; };
   if (n >= N) {
-    for (int g = lane; g < G; g += 32) prm[(size_t)g * n_pad + n] = make_uint2(0, 0);
+    for (int g = lane; g < Gp; g += 32) at(g) = make_uint2(0, 0);
     return;
   }
   float ms = 0.0f, mw = 0.0f;
@@ -321,8 +412,9 @@ __global__ void __launch_bounds__(256) w_prep_kernel(const uint16_t* __restrict_
     uint2 o;
     o.x = *reinterpret_cast<const uint32_t*>(&sv);
     o.y = (uint32_t)__half_as_ushort(bv);
-    prm[(size_t)g * n_pad + n] = o;
+    at(g) = o;
   }
+  if (lane == 0 && Gp != G) at(G) = make_uint2(0, 0);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -345,6 +437,11 @@ static EncodeTiledFn encode_fn() {
 
 int qmm_row_pad(int N) { return (N + tc::BM - 1) / tc::BM * tc::BM; }
 
+size_t qmm_prm_bytes(int N, int K) {
+  const size_t groups = (size_t)((K / 64 + 1) & ~1);
+  return (size_t)qmm_row_pad(N) * groups * sizeof(uint2);
+}
+
 int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm, int N, int K, cudaStream_t stream) {
   const int threads = 256;
   const int n_pad = qmm_row_pad(N);
@@ -363,36 +460,53 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
   int* status = device_status_ptr();
   if (!status) return fail(QVX_ERR_CUDA, "qvx_qmm: device status word unavailable");
   const cuuint32_t estride[2] = {1, 1};
-  // x16 [M, K] fp16: 64 x 128 boxes, 128-byte swizzle (the MMA's K-major B layout)
+  // x16 [M, K] fp16: 64 x 128 boxes, 128-byte swizzle (the MMA's K-major B layout); a
+  // box starting at K (odd group count) reads zeros
   CUtensorMap tmap_x;
   const cuuint64_t xdim[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t xstride[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t xbox[2] = {BK, BN};
+  const cuuint32_t xbox[2] = {64, BN};
   CUresult r = enc(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), xdim, xstride, xbox, estride,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QVX_ERR_CUDA, "qvx_qmm: x tensor map encode failed (%d)", (int)r);
-  // w [N, K/8] uint32: 8-word x 256-row boxes (one K step of a tile), rows past N read as 0
+  // w [N, K/8] uint32: 16-word x 256-row boxes (one stage of a tile), 64-byte swizzle so the
+  // dequantisers' row reads are bank-conflict free; rows past N and words past K/8 read 0
   CUtensorMap tmap_w;
   const cuuint64_t wdim[2] = {(cuuint64_t)(K / 8), (cuuint64_t)N};
   const cuuint64_t wstride[1] = {(cuuint64_t)K / 2};
   const cuuint32_t wbox[2] = {BK / 8, BM};
   r = enc(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), wdim, wstride, wbox, estride,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QVX_ERR_CUDA, "qvx_qmm: w tensor map encode failed (%d)", (int)r);
-  static bool attr_set[64] = {};
+  // y [M, N] bf16 written by 256 x 128 TMA stores (clipped at the edges) when its rows are
+  // 16-byte multiples; otherwise the epilogue stores elements directly
+  const bool staged = (N % 8 == 0) && aligned(y, 16);
+  CUtensorMap tmap_y;
+  memset(&tmap_y, 0, sizeof(tmap_y));
+  if (staged) {
+    const cuuint64_t ydim[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    const cuuint64_t ystride[1] = {(cuuint64_t)N * 2};
+    const cuuint32_t ybox[2] = {BM, BN};
+    r = enc(&tmap_y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, ydim, ystride, ybox, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(QVX_ERR_CUDA, "qvx_qmm: y tensor map encode failed (%d)", (int)r);
+  }
+  auto kern = staged ? qmm_tc_kernel<true> : qmm_tc_kernel<false>;
+  static bool attr_set[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    if (cudaFuncSetAttribute(qmm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+  if (dev < 0 || dev >= 64 || !attr_set[dev][staged]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
       return fail(QVX_ERR_CUDA, "qvx_qmm: cannot set shared memory size");
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev][staged] = true;
   }
   const int ntiles = ((M + BN - 1) / BN) * ((N + BM - 1) / BM);
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  qmm_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap_x, tmap_w, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N),
-                                                       status);
+  kern<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap_x, tmap_w, tmap_y, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N),
+                                             status);
   return check_launch("qvx_qmm");
 }
 

@@ -106,6 +106,23 @@ __device__ __forceinline__ void tma_tile_2d_g2s(uint32_t dst_smem, const void* t
       : "memory");
 }
 
+// 2-D tiled tensor copy shared -> global (bulk-group completion; elements past the tensor's
+// bounds are not written).  The generic-proxy writes that produced the tile must be made
+// visible to the async proxy first (fence_proxy_async_smem by every writing thread).
+__device__ __forceinline__ void tma_tile_2d_s2g(const void* tmap, uint32_t src_smem, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(src_smem), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk group of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every committed bulk group of this thread has completed (writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
