@@ -76,6 +76,21 @@ int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* bi
             void* y, int M, int N, int K, int group_size, int bits, void* workspace,
             size_t workspace_bytes, void* stream);
 
+/* qvx_qmm for callers that cannot allocate device memory: no counterpart in the
+ * reference, which runs on MLX's own allocator.  It is meant for hosts that reach this
+ * library only through the C ABI with no device allocator of their own, and for engines
+ * whose memory pool owns the GPU's memory and forbids cudaMalloc while serving.  The
+ * scratch qvx_qmm would take as a workspace is a 16 MiB array built into the library,
+ * held by every GPU that loads it until the process exits.  Calls whose
+ * qvx_qmm_workspace_size(M, N, K) exceeds 16 MiB fail with QVX_ERR_WORKSPACE; at
+ * N = 12288, K = 4096 that is above about M = 1270.  Same results as qvx_qmm.  Every
+ * call shares the array, so calls that overlap on the GPU (other streams, other host
+ * threads) race: order them.  Nothing in it needs clearing, since each call writes all
+ * the scratch it reads.  The first call on each device looks up the array's address;
+ * make it before any stream capture. */
+int qvx_qmm_noalloc(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                    void* y, int M, int N, int K, int group_size, int bits, void* stream);
+
 /* Dispatcher with mx.quantized_matmul's semantics: qvx_qmv for M <= 8, qvx_qmm above.
  * The workspace may be NULL when M <= 8. */
 int qvx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,

@@ -32,6 +32,7 @@ SIGNATURES = {
     "qvx_qmv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_qmm_workspace_size": (_SZ, [_I, _I, _I]),
     "qvx_qmm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+    "qvx_qmm_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_quantized_matmul": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "qvx_quantize": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_dequantize": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
