@@ -35,8 +35,9 @@
 namespace qvx {
 
 constexpr int kStreamMaxComputeWarps = 12;
-// Shared memory per CTA: kept under half of the SM so that two launches are co-resident.
-constexpr size_t kStreamSmemBudget = 105 * 1024;
+// Shared memory per CTA: kept under half of the SM (228 KB, 1 KB of it reserved per CTA)
+// so that two launches are co-resident.
+constexpr size_t kStreamSmemBudget = 112 * 1024;
 constexpr int kStreamMaxStages = 8;
 // Codes per stage: measured on B200, 16 KB stages (4 rows per team at K = 4096) stream
 // lm_head at ~80% of HBM against ~63% for 8 KB stages.
@@ -100,27 +101,26 @@ __device__ __forceinline__ void make_planes(const float (&xf)[32], XPlanes& xp) 
   }
   int E = 0;
   if (mx > 0.0f && isfinite(mx)) frexpf(mx, &E);  // 2^(E-1) <= mx < 2^E
-  E = max(E, -100);
-  const float up = ldexpf(1.0f, 22 - E);
-  xp.scale = ldexpf(1.0f, E - 22);
+  E = max(E, -100);                                // E <= 128, so both powers below are normal
+  const float up = __int_as_float((22 - E + 127) << 23);   // 2^(22-E)
+  xp.scale = __int_as_float((E - 22 + 127) << 23);         // 2^(E-22)
   xp.xsum = sum;
 #pragma unroll
   for (int w = 0; w < 4; ++w)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      uint32_t b0 = 0, b1 = 0, b2 = 0;
+      uint32_t v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 4; ++i)
         // x * 2^(22-E) has |.| < 2^22, so adding 1.5 * 2^23 lands in [2^23, 2^24) where the
         // float spacing is 1: one FFMA rounds to the nearest integer, exactly
-        const int v = __float_as_int(fmaf(xf[8 * w + h + 2 * i], up, 12582912.0f)) - 0x4B400000;
-        b0 |= ((uint32_t)v & 0xFFu) << (8 * i);
-        b1 |= (((uint32_t)v >> 8) & 0xFFu) << (8 * i);
-        b2 |= (((uint32_t)v >> 16) & 0xFFu) << (8 * i);
+        v[i] = (uint32_t)(__float_as_int(fmaf(xf[8 * w + h + 2 * i], up, 12582912.0f)) - 0x4B400000);
+      // byte j of the four values -> plane j, three PRMTs per plane
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const uint32_t sel = 0x0040u + 0x0011u * (uint32_t)j;  // (v_a byte j, v_b byte j)
+        xp.pl[j][2 * w + h] = __byte_perm(__byte_perm(v[0], v[1], sel), __byte_perm(v[2], v[3], sel), 0x5410);
       }
-      xp.pl[0][2 * w + h] = b0;
-      xp.pl[1][2 * w + h] = b1;
-      xp.pl[2][2 * w + h] = b2;
     }
 }
 
@@ -345,15 +345,19 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   while (rt > 1 && (size_t)T * rt * K / 2 > kStreamStageCodeBytes) rt /= 2;
   const int mc = M == 1 ? 1 : 2;  // x costs 24 registers per token
   const bool fullk = K % 1024 == 0;
-  // ring depth: 4 stages of ~16 KB, or 6 when the stages are smaller (both fit the budget)
-  const bool deep = 6 * (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)) + 16 <= kStreamSmemBudget;
-#define QVX_STREAM_CASE(MC_, RT_)                                                                             \
-  if (mc == MC_ && rt == RT_) {                                                                               \
-    if (deep)                                                                                                 \
-      return fullk ? launch_stream<MC_, RT_, true, 6>(T, x, w, s, b, y, M, N, K, stream, status)              \
-                   : launch_stream<MC_, RT_, false, 6>(T, x, w, s, b, y, M, N, K, stream, status);            \
-    return fullk ? launch_stream<MC_, RT_, true, 4>(T, x, w, s, b, y, M, N, K, stream, status)                \
-                 : launch_stream<MC_, RT_, false, 4>(T, x, w, s, b, y, M, N, K, stream, status);              \
+  // ring depth: as many stages (4..7) as the shared-memory budget holds
+  int depth = (int)((kStreamSmemBudget - 16) / (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)));
+  depth = depth < 4 ? 4 : depth > 7 ? 7 : depth;
+#define QVX_STREAM_S(MC_, RT_, S_)                                                                          \
+  if (depth == S_)                                                                                          \
+    return fullk ? launch_stream<MC_, RT_, true, S_>(T, x, w, s, b, y, M, N, K, stream, status)             \
+                 : launch_stream<MC_, RT_, false, S_>(T, x, w, s, b, y, M, N, K, stream, status);
+#define QVX_STREAM_CASE(MC_, RT_)                                                                           \
+  if (mc == MC_ && rt == RT_) {                                                                             \
+    QVX_STREAM_S(MC_, RT_, 4)                                                                               \
+    QVX_STREAM_S(MC_, RT_, 5)                                                                               \
+    QVX_STREAM_S(MC_, RT_, 6)                                                                               \
+    QVX_STREAM_S(MC_, RT_, 7)                                                                               \
   }
   QVX_STREAM_CASE(1, 4)
   QVX_STREAM_CASE(1, 2)
@@ -362,6 +366,7 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   QVX_STREAM_CASE(2, 2)
   QVX_STREAM_CASE(2, 1)
 #undef QVX_STREAM_CASE
+#undef QVX_STREAM_S
   return fail(QVX_ERR_UNSUPPORTED, "qvx_qmv: no streaming plan for M=%d K=%d", M, K);
 }
 
