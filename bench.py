@@ -11,8 +11,11 @@ launches carry programmatic-dependent-launch edges).  The weights total 4.46 GB,
 above the 126 MB L2, so no flush is needed between steps.
 
 With --gpus N (torchrun, one rank per GPU) each projection is column-sharded: rank r
-owns a contiguous 1/N of the output rows (weights, scales, biases) and the shards are
-all-gathered over NCCL after each projection (strong scaling: total work fixed).
+owns a contiguous 1/N of the output rows (weights, scales, biases), and the shards are
+all-gathered after each projection (strong scaling: total work fixed): over NCCL by
+default, or with --gather fused inside the qmv kernel (qvx_qmv_allgather: every rank
+stores its rows into every rank's output buffer over NVLink and signals; no NCCL call
+inside the step).
 
 Prints ONE JSON line (rank 0).  `--impl reference` times the reference's arithmetic on
 the host CPU cores instead (the oracle port of engine/kernels.py's qmv arithmetic: MLX,
@@ -47,6 +50,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=1, help="tokens per step (1 = batch-1 decode)")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers (32 = the full 9B shape)")
+    ap.add_argument("--gather", choices=("fused", "nccl"), default="nccl",
+                    help="N>1: all-gather fused into the qmv kernel (peer stores over NVLink) or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the M=2/4/8 side measurements")
     ap.add_argument("--no-configs", action="store_true",
@@ -314,14 +319,27 @@ def run_ours(args):
     g.manual_seed(1234)
     xs = {K: torch.randn((M, K), device=device, generator=g).to(torch.bfloat16) for K in Ks}
     local_out = [torch.empty((M, l.out_features), dtype=torch.bfloat16, device=device) for _, _, _, l in lins]
-    full_out = [torch.empty((world, M, N // world), dtype=torch.bfloat16, device=device) for _, N, _, _ in lins]
     launches_per_step = len(lins)
+    fused = world > 1 and args.gather == "fused"
+    peer = None
+    if fused:
+        # one output region per projection on every rank, mapped everywhere (CUDA IPC)
+        from qvex.shard import PeerGather, qmv_allgather
+        peer = PeerGather([M * N * 2 for _, N, _, _ in lins])
+        descs = [peer.descriptor(i, N, rank * (N // world)) for i, (_, N, _, _) in enumerate(lins)]
+        full_out = [peer.output(i, M, N) for i, (_, N, _, _) in enumerate(lins)]
+    else:
+        full_out = [torch.empty((world, M, N // world), dtype=torch.bfloat16, device=device) for _, N, _, _ in lins]
 
     def step_qmv():
         for (_, _, K, lin), out in zip(lins, local_out):
             lin(xs[K], out=out)
 
     def step_full():
+        if fused:
+            for (_, _, K, lin), d in zip(lins, descs):
+                qmv_allgather(lin, xs[K], d)
+            return
         for (_, _, K, lin), out, full in zip(lins, local_out, full_out):
             lin(xs[K], out=out)
             if world > 1:
@@ -333,6 +351,8 @@ def run_ours(args):
         torch.cuda.synchronize()
         if rank == 0:
             print(json.dumps({"profile_run": True, "launches_per_step": launches_per_step}))
+        if peer is not None:
+            peer.close()
         if world > 1:
             dist.destroy_process_group()
         return
@@ -466,7 +486,9 @@ def run_ours(args):
             "data": "synthetic (seeded codes/scales/biases as config 0; x ~ N(0,1))",
             "config": {"workload": "config 1: all 145 4-bit g64 linears of one Qwen3.5-9B-shaped decode step",
                        "M": M, "layers": args.layers, "weight_bytes_per_step": weight_bytes,
-                       "parallelism": f"column-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"column-shard x{world} + all-gather fused into the qmv kernel (NVLink peer stores)"
+                                       if fused else f"column-shard x{world} + NCCL all-gather"),
                        "l2": "inputs larger than L2 (4.46 GB of weights per step)", "cuda_graph": True},
             "tok_per_s": round(1000.0 / ms_step, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -487,6 +509,8 @@ def run_ours(args):
             rec["cpu_baseline"] = cpu
         print(json.dumps(rec))
     del graph_full, graph_q
+    if peer is not None:
+        peer.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -91,6 +91,42 @@ int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* bi
 int qvx_qmm_noalloc(const void* x, const uint32_t* w, const void* scales, const void* biases,
                     void* y, int M, int N, int K, int group_size, int bits, void* stream);
 
+/* ---------------------------------------------------------------- column-sharded decode */
+
+#define QVX_MAX_RANKS 8
+
+/* Where the outputs of a column-sharded projection go.  Every rank r holds a full output
+ * buffer out[r] (bf16 [M, n_total], row stride n_total) and an array of 32-bit signal
+ * words indexed by slot; out[] and signal[] are those buffers as mapped in the calling
+ * process (peer mappings such as CUDA IPC for r != rank, reachable over NVLink).  epoch
+ * points to this rank's own launch counters in device memory, also indexed by slot; the
+ * signal words and the epochs start at zero.  slot names the projection: two projections
+ * must not share one. */
+typedef struct qvx_gather {
+  void* out[QVX_MAX_RANKS];
+  unsigned int* signal[QVX_MAX_RANKS];
+  unsigned int* epoch;
+  int world;   /* ranks, 1..QVX_MAX_RANKS */
+  int rank;    /* this rank */
+  int n_total; /* rows of the whole projection */
+  int row0;    /* first row of this rank's shard */
+  int slot;    /* signal word and epoch index */
+} qvx_gather;
+
+/* Column-sharded decode projection with its all-gather fused in: y = x @ dequant(w)^T
+ * for this rank's N rows (global rows row0 .. row0+N-1), written into rows [row0, row0+N)
+ * of EVERY rank's out buffer by peer stores, then signalled.  When the kernel completes,
+ * out[rank] holds all n_total outputs of all ranks.  Replaces the per-projection
+ * qvx_qmv + NCCL all-gather of column sharding (the reference runs on one Apple GPU and
+ * has no counterpart; the projection it shards is QLinear.__call__, engine/model.py:87-91).
+ * Every rank must make the same sequence of calls with the same M, N and K.  M <= 8,
+ * K % 512 == 0, scales/biases and every out[r] 16-byte aligned.  A rank that never
+ * arrives makes the others give up after 2 s with QVX_ERR_TIMEOUT in the device status
+ * word. */
+int qvx_qmv_allgather(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                      const qvx_gather* g, int M, int N, int K, int group_size, int bits,
+                      void* stream);
+
 /* Dispatcher with mx.quantized_matmul's semantics: qvx_qmv for M <= 8, qvx_qmm above.
  * The workspace may be NULL when M <= 8. */
 int qvx_quantized_matmul(const void* x, const uint32_t* w, const void* scales,

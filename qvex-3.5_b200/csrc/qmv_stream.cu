@@ -30,6 +30,8 @@
 //     sum q * p_j in int32 (no overflow: 15*255*32 < 2^17);
 //   * per row: Q = a0 + 256 a1 + 65536 a2, sum(q x) = 2^(E-22) Q, and the group term of the
 //     reference factorisation s*sum(q x) + b*sum(x) (engine/kernels.py:151-171).
+#include <cstring>
+
 #include "sm100.cuh"
 
 namespace qvx {
@@ -38,7 +40,6 @@ constexpr int kStreamMaxComputeWarps = 12;
 // Shared memory per CTA: kept under half of the SM (228 KB, 1 KB of it reserved per CTA)
 // so that two launches are co-resident.
 constexpr size_t kStreamSmemBudget = 112 * 1024;
-constexpr int kStreamMaxStages = 8;
 // Codes per stage: measured on B200, 16 KB stages (4 rows per team at K = 4096) stream
 // lm_head at ~80% of HBM against ~63% for 8 KB stages.
 constexpr size_t kStreamStageCodeBytes = 16384;
@@ -71,6 +72,37 @@ __device__ __forceinline__ void reduce_transpose(float* p, int lane) {
       reduce_transpose<1, OFF / 2>(p, lane);
     }
   }
+}
+
+// Destination of the fused column-sharded form (qvx_qmv_allgather); world == 0 for the
+// plain qvx_qmv form.  A copy of qvx_gather in the kernel's parameter space.
+struct QmvGather {
+  __nv_bfloat16* out[QVX_MAX_RANKS];
+  unsigned* signal[QVX_MAX_RANKS];
+  unsigned* epoch;
+  int world, rank, n_total, row0, slot;
+};
+
+__device__ __forceinline__ void red_add_release_sys(unsigned* addr, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// dst[0, n) = src[0, n) by one warp; dst and src have the same address mod 16 (every
+// rank's buffer has the same layout and a 256-byte aligned base)
+__device__ __forceinline__ void copy_bf16_segment(__nv_bfloat16* dst, const __nv_bfloat16* src, int n, int lane) {
+  const int head = min(n, (int)(((16u - ((uint32_t)reinterpret_cast<uintptr_t>(src) & 15u)) & 15u) >> 1));
+  if (lane < head) dst[lane] = src[lane];
+  const int nv = (n - head) >> 3;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + head);
+  uint4* d4 = reinterpret_cast<uint4*>(dst + head);
+  for (int i = lane; i < nv; i += 32) d4[i] = s4[i];
+  const int done = head + nv * 8;
+  if (lane < n - done) dst[done + lane] = src[done + lane];
 }
 
 __device__ __forceinline__ uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
@@ -128,7 +160,7 @@ template <int MC, int RT, bool FULLK, int S>
 __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     qmv_stream_kernel(const __nv_bfloat16* __restrict__ x, const uint32_t* __restrict__ w,
                       const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, __nv_bfloat16* __restrict__ y,
-                      int M, int N, int K, int T, int* status) {
+                      int M, int N, int K, int T, int* status, const QmvGather g) {
   using VC = VCfg<RT * MC>;
   constexpr int V = VC::V, LV = VC::LV;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -151,6 +183,9 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
   const int r_end = (int)(((long long)(blockIdx.x + 1) * N) / gridDim.x);
   const int nchunks = (r_end - r_begin + R - 1) / R;
 
+  const bool gather = g.world > 0;
+  // thread 0 is a compute thread, so it has passed griddepcontrol.wait before it waits here
+  const bool gather_waiter = gather && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -280,19 +315,61 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
         if (r < nr && m < mc) {
           float acc = 0.0f;
           for (int p = 0; p < P; ++p) acc += red[(team * P + p) * 32 + idx];
-          y[(size_t)(m0 + m) * N + r0 + r] = __float2bfloat16_rn(acc);
+          const __nv_bfloat16 yv = __float2bfloat16_rn(acc);
+          if (gather) {
+            // this rank's own full output; the peers get the CTA's rows once, at the end
+            // (a peer store here would make every stage release wait for NVLink)
+            g.out[g.rank][(size_t)(m0 + m) * g.n_total + g.row0 + r0 + r] = yv;
+          } else {
+            y[(size_t)(m0 + m) * N + r0 + r] = yv;
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (gather) {
+      // copy this CTA's row segment of each token to every peer (16-byte stores over
+      // NVLink), then publish it to every rank -- also after an abort, so that the others
+      // do not wait out their timeout for this rank
+      __syncwarp();
+      const int nrows = r_end - r_begin;
+      for (int m = 0; m < mc; ++m) {
+        const size_t at = (size_t)(m0 + m) * g.n_total + g.row0 + r_begin;
+        for (int q = 0; q < g.world; ++q)
+          if (q != g.rank) copy_bf16_segment(g.out[q] + at, g.out[g.rank] + at, nrows, lane);
+      }
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0)
+        for (int q = 0; q < g.world; ++q) red_add_release_sys(g.signal[q] + g.slot, 1u);
+    }
   }
   __syncthreads();
+  if (gather_waiter) {
+    // the grid completes only once every CTA of every rank has published this launch, so
+    // completion of the kernel means out[rank] holds all n_total rows.  The slot's launch
+    // count is read after griddepcontrol.wait: an earlier launch of the same slot may be the
+    // kernel this one overlapped with.
+    const unsigned epoch0 = *reinterpret_cast<volatile unsigned*>(g.epoch + g.slot);
+    const unsigned target = (epoch0 + 1u) * (unsigned)g.world * gridDim.x * gridDim.y;
+    const unsigned* sig = g.signal[g.rank] + g.slot;
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      if ((int)(ld_acquire_sys(sig) - target) >= 0) break;
+      if ((it & 63) == 0 && (globaltimer_ns() - t0 > kWaitTimeoutNs || it > kWaitMaxPolls)) {
+        set_device_status(status, QVX_ERR_TIMEOUT);
+        break;
+      }
+    }
+    g.epoch[g.slot] = epoch0 + 1u;
+    __threadfence();
+  }
 }
 
 template <int MC, int RT, bool FULLK, int S>
 static int launch_stream(int T, const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M,
-                         int N, int K, cudaStream_t stream, int* status) {
+                         int N, int K, cudaStream_t stream, int* status, const QmvGather& g) {
   auto kern = qmv_stream_kernel<MC, RT, FULLK, S>;
   const int P = (K + 1023) / 1024;
   const int threads = (T * P + 2) * 32;
@@ -326,7 +403,7 @@ static int launch_stream(int T, const void* x, const uint32_t* w, const void* s,
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const __nv_bfloat16*>(x), w,
                                      static_cast<const uint16_t*>(s), static_cast<const uint16_t*>(b),
-                                     static_cast<__nv_bfloat16*>(y), M, N, K, T, status);
+                                     static_cast<__nv_bfloat16*>(y), M, N, K, T, status, g);
   if (e != cudaSuccess) return fail(QVX_ERR_CUDA, "qvx_qmv launch: %s", cudaGetErrorString(e));
   return QVX_OK;
 }
@@ -334,7 +411,10 @@ static int launch_stream(int T, const void* x, const uint32_t* w, const void* s,
 // Returns QVX_OK after launching, or -1 when the streaming kernel does not apply
 // (the caller then uses the general kernel).
 int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const QmvGather* gather) {
+  QmvGather g;
+  memset(&g, 0, sizeof(g));
+  if (gather) g = *gather;
   if (K % 512 != 0 || K > kStreamMaxComputeWarps * 1024 || !aligned(s, 16) || !aligned(b, 16)) return -1;
   int* status = device_status_ptr();
   if (!status) return fail(QVX_ERR_CUDA, "qvx_qmv: device status word unavailable");
@@ -350,8 +430,8 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   depth = depth < 4 ? 4 : depth > 7 ? 7 : depth;
 #define QVX_STREAM_S(MC_, RT_, S_)                                                                          \
   if (depth == S_)                                                                                          \
-    return fullk ? launch_stream<MC_, RT_, true, S_>(T, x, w, s, b, y, M, N, K, stream, status)             \
-                 : launch_stream<MC_, RT_, false, S_>(T, x, w, s, b, y, M, N, K, stream, status);
+    return fullk ? launch_stream<MC_, RT_, true, S_>(T, x, w, s, b, y, M, N, K, stream, status, g)             \
+                 : launch_stream<MC_, RT_, false, S_>(T, x, w, s, b, y, M, N, K, stream, status, g);
 #define QVX_STREAM_CASE(MC_, RT_)                                                                           \
   if (mc == MC_ && rt == RT_) {                                                                             \
     QVX_STREAM_S(MC_, RT_, 4)                                                                               \
@@ -370,4 +450,42 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   return fail(QVX_ERR_UNSUPPORTED, "qvx_qmv: no streaming plan for M=%d K=%d", M, K);
 }
 
+int check_qparams(const char* who, const void* x, const uint32_t* w, const void* s, const void* b, const void* y,
+                  int M, int N, int K, int group_size, int bits);
+
 }  // namespace qvx
+
+extern "C" int qvx_qmv_allgather(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                                 const qvx_gather* g, int M, int N, int K, int group_size, int bits, void* stream) {
+  using namespace qvx;
+  if (!g) return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: null gather descriptor");
+  if (g->world < 1 || g->world > QVX_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+    return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: rank %d of world %d (1..%d ranks)", g->rank, g->world,
+                QVX_MAX_RANKS);
+  if (g->slot < 0 || g->row0 < 0 || (long long)g->row0 + N > (long long)g->n_total)
+    return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: rows [%d, %d) outside the %d-row projection (slot %d)",
+                g->row0, g->row0 + N, g->n_total, g->slot);
+  for (int q = 0; q < g->world; ++q)
+    if (!g->out[q] || !g->signal[q] || !aligned(g->out[q], 16) || !aligned(g->signal[q], 4))
+      return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: missing or misaligned buffer of rank %d", q);
+  if (!g->epoch || !aligned(g->epoch, 4)) return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: missing epoch counters");
+  int rc = check_qparams("qvx_qmv_allgather", x, w, scales, biases, g->out[g->rank], M, N, K, group_size, bits);
+  if (rc) return rc;
+  if (M > 8) return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: M=%d > 8", M);
+  QmvGather d;
+  for (int q = 0; q < QVX_MAX_RANKS; ++q) {
+    d.out[q] = q < g->world ? static_cast<__nv_bfloat16*>(g->out[q]) : nullptr;
+    d.signal[q] = q < g->world ? g->signal[q] : nullptr;
+  }
+  d.epoch = g->epoch;
+  d.world = g->world;
+  d.rank = g->rank;
+  d.n_total = g->n_total;
+  d.row0 = g->row0;
+  d.slot = g->slot;
+  rc = qmv_stream_try(x, w, scales, biases, g->out[g->rank], M, N, K, static_cast<cudaStream_t>(stream), &d);
+  if (rc < 0)
+    return fail(QVX_ERR_UNSUPPORTED, "qvx_qmv_allgather: needs K %% 512 == 0, K <= 12288 and 16-byte aligned "
+                "scales/biases (K=%d)", K);
+  return rc;
+}

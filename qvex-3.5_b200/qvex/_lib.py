@@ -33,12 +33,23 @@ SIGNATURES = {
     "qvx_qmm_workspace_size": (_SZ, [_I, _I, _I]),
     "qvx_qmm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "qvx_qmm_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "qvx_qmv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_quantized_matmul": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "qvx_quantize": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_dequantize": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "qvx_dequantize_rows": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "qvx_gated_delta": (_I, [_P] * 11 + [_I] * 6 + [_P]),
 }
+
+
+QVX_MAX_RANKS = 8
+
+
+class QvxGather(ctypes.Structure):
+    """Mirror of ``qvx_gather`` (include/qvex.h): peer output buffers and signal words of
+    a column-sharded projection, this rank's epoch counters, and its place in the rows."""
+    _fields_ = [("out", _P * QVX_MAX_RANKS), ("signal", _P * QVX_MAX_RANKS), ("epoch", _P),
+                ("world", _I), ("rank", _I), ("n_total", _I), ("row0", _I), ("slot", _I)]
 
 
 class QvexError(RuntimeError):

@@ -7,11 +7,20 @@ y.  Fused projections are sharded per component (``shard_fused``) so that a
 nonlinearity that pairs components -- SwiGLU over gate|up, the DeltaNet split of
 qkv|z|b|a -- finds both halves of its inputs on the same rank.
 
+For decode (M <= 8) the all-gather can instead be fused into the projection kernel
+(``qvx_qmv_allgather``): every rank stores its rows straight into every rank's output
+buffer over NVLink and signals a per-projection counter, so one kernel per projection
+does the compute and the exchange, with no NCCL call.  ``PeerGather`` sets up those
+buffers: one device allocation per rank, mapped into every rank's process with CUDA IPC.
+
 The pieces are separate so the host logic runs on CPU process groups (gloo) in tests:
 ``shard_rows`` / ``shard_linear`` / ``shard_fused`` only slice, ``gather_columns`` only
-moves data, ``ShardedQLinear`` composes them with the CUDA kernel.
+moves data, ``plan_gather_layout`` / ``gather_descriptor`` only compute offsets and
+addresses, ``ShardedQLinear`` composes them with the CUDA kernels.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -65,18 +74,172 @@ def gather_columns(local_y: torch.Tensor, group=None, out: torch.Tensor | None =
     return y.reshape(*lead, world * n_loc)
 
 
+GATHER_ALIGN = 256
+GATHER_M_MAX = 8  # tokens a fused decode projection gathers (qvx_qmv's M <= 8)
+
+
+def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], int]:
+    """Byte layout of one rank's PeerGather buffer: a 32-bit signal word per region (slot),
+    padded to 256 bytes, then the regions, each 256-byte aligned.  Returns the regions'
+    offsets and the total size."""
+    if any(b <= 0 for b in region_bytes):
+        raise ValueError("every region needs a positive size")
+
+    def up(v):
+        return (v + GATHER_ALIGN - 1) // GATHER_ALIGN * GATHER_ALIGN
+
+    at = up(4 * len(region_bytes))
+    offsets = []
+    for b in region_bytes:
+        offsets.append(at)
+        at = up(at + b)
+    return offsets, at
+
+
+def gather_descriptor(bases: list[int], offset: int, epoch_ptr: int, rank: int, slot: int, n_total: int,
+                      row0: int):
+    """qvx_gather for one projection: out[r] = rank r's buffer + the slot's region offset;
+    signal[r] = rank r's buffer itself (the signal words lead it and the kernel indexes
+    them by slot); epoch = this rank's counters (also indexed by slot in the kernel)."""
+    from . import _lib
+    d = _lib.QvxGather()
+    for r, base in enumerate(bases):
+        d.out[r] = base + offset
+        d.signal[r] = base
+    d.epoch = epoch_ptr
+    d.world, d.rank, d.n_total, d.row0, d.slot = len(bases), rank, n_total, row0, slot
+    return d
+
+
+def _ck(res):
+    """Unwrap a cuda-python (error, value...) result, raising on an error."""
+    err, *vals = res if isinstance(res, tuple) else (res,)
+    if int(err) != 0:
+        raise RuntimeError(f"CUDA runtime call failed: {err}")
+    return vals[0] if len(vals) == 1 else (tuple(vals) if vals else None)
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ over a raw device pointer (torch.as_tensor wraps it)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...]):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGather:
+    """Output regions and signal words of fused column-sharded projections, one device
+    buffer per rank of ``group`` mapped into every rank's process (CUDA IPC; peer access
+    over NVLink).  ``region_bytes[i]`` is the size of slot i's full output; every rank must
+    construct it with the same list, and keep it alive while its projections are in use.
+    Set-up allocates and exchanges handles; the projections themselves allocate nothing."""
+
+    def __init__(self, region_bytes: list[int], group=None):
+        from cuda.bindings import runtime as rt
+        from . import _lib
+        self._rt = rt
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _lib.QVX_MAX_RANKS:
+            raise ValueError(f"{self.world} ranks; the fused gather supports up to {_lib.QVX_MAX_RANKS}")
+        self.device = torch.cuda.current_device()
+        _ck(rt.cudaSetDevice(self.device))
+        self.offsets, self.nbytes = plan_gather_layout(region_bytes)
+        self.slots = len(region_bytes)
+        self._own = _ck(rt.cudaMalloc(self.nbytes))
+        _ck(rt.cudaMemset(self._own, 0, self.nbytes))
+        _ck(rt.cudaDeviceSynchronize())
+        handle = _ck(rt.cudaIpcGetMemHandle(self._own))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.reserved), group=group)
+        self.base = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                self.base.append(int(self._own))
+            else:
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = hb
+                self.base.append(int(_ck(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))))
+        self.epoch = torch.zeros(max(1, self.slots), dtype=torch.int32, device=self.device)
+        self._next = 0
+        dist.barrier(group)  # every rank has mapped every buffer before anyone stores
+
+    def reserve(self) -> int:
+        """Hands out the next slot."""
+        if self._next >= self.slots:
+            raise ValueError(f"all {self.slots} gather slots are taken")
+        self._next += 1
+        return self._next - 1
+
+    def descriptor(self, slot: int, n_total: int, row0: int):
+        return gather_descriptor(self.base, self.offsets[slot], self.epoch.data_ptr(), self.rank, slot, n_total,
+                                 row0)
+
+    def output(self, slot: int, M: int, n_total: int) -> torch.Tensor:
+        """This rank's full output of ``slot`` as a bf16 [M, n_total] tensor (a view of the
+        shared buffer: the next call of that projection overwrites it)."""
+        arr = _DeviceArray(self.base[self.rank] + self.offsets[slot], (M, n_total))
+        return torch.as_tensor(arr, device=f"cuda:{self.device}").view(torch.bfloat16)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (after a device sync and a
+        barrier, so no rank still stores into it)."""
+        if self._own is None:
+            return
+        rt = self._rt
+        _ck(rt.cudaDeviceSynchronize())
+        dist.barrier(self.group)
+        for r, p in enumerate(self.base):
+            if r != self.rank:
+                _ck(rt.cudaIpcCloseMemHandle(p))
+        dist.barrier(self.group)
+        _ck(rt.cudaFree(self._own))
+        self._own = None
+
+
+def qmv_allgather(local: QLinear, x: torch.Tensor, desc) -> None:
+    """One fused launch: this rank's rows of ``local`` times x [M <= 8, K], stored into every
+    rank's output region of ``desc`` (a PeerGather descriptor) and signalled."""
+    from . import _lib
+    if x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise ValueError("x must be a bf16 CUDA tensor")
+    x = x.contiguous()
+    M, K = x.shape
+    w, s, b = local.w, local.scales, local.biases
+    P = ctypes.c_void_p
+    rc = _lib.lib().qvx_qmv_allgather(P(x.data_ptr()), P(w.data_ptr()), P(s.data_ptr()), P(b.data_ptr()),
+                                      ctypes.byref(desc), M, w.shape[0], K, local.group_size, local.bits,
+                                      P(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc, "qvx_qmv_allgather")
+
+
 class ShardedQLinear:
-    """A QLinear whose output rows are spread over the ranks of ``group``."""
+    """A QLinear whose output rows are spread over the ranks of ``group``.
+
+    With ``peer`` (a PeerGather) decode calls (M <= 8) run the fused kernel: compute and
+    all-gather in one launch, returning a view of the gathered output.  Otherwise, and for
+    M > 8, the local kernel is followed by an NCCL all-gather."""
 
     def __init__(self, full: QLinear | list[QLinear], group=None, rank: int | None = None,
-                 world: int | None = None):
+                 world: int | None = None, peer: PeerGather | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if world is None else world
         self.rank = dist.get_rank(group) if rank is None else rank
         parts = full if isinstance(full, list) else [full]
         self.local = shard_fused(parts, self.world, self.rank)
         self.out_features = sum(p.w.shape[0] for p in parts)
+        self.peer = peer
+        if peer is not None:
+            self.slot = peer.reserve()
+            n_loc = self.local.w.shape[0]
+            self._desc = peer.descriptor(self.slot, self.out_features, self.rank * n_loc)
 
     def __call__(self, x: torch.Tensor, *, gather: bool = True) -> torch.Tensor:
+        x2 = x.reshape(-1, x.shape[-1])
+        if self.peer is not None and gather and x2.shape[0] <= GATHER_M_MAX:
+            qmv_allgather(self.local, x2, self._desc)
+            return self.peer.output(self.slot, x2.shape[0], self.out_features).reshape(*x.shape[:-1],
+                                                                                        self.out_features)
         y = self.local(x)
         return gather_columns(y, self.group) if gather and self.world > 1 else y

@@ -114,3 +114,31 @@ def test_qlinear_fuse_and_rollback_host_logic():
     c.ssm_prev, c.conv_prev = "s0", "c0"
     c.rollback(1)
     assert (c.ssm, c.conv, c.offset, c.ssm_prev) == ("s0", "c0", 4, None)
+
+
+def test_qmv_allgather_rejects_bad_descriptors(L):
+    from qvex import _lib
+    g = _lib.QvxGather()
+    for r in range(2):
+        g.out[r] = 4096
+        g.signal[r] = 4096
+    g.epoch = 4096
+    g.world, g.rank, g.n_total, g.row0, g.slot = 2, 0, 16, 0, 0
+
+    def call(gg, M=1, N=8):
+        return L.qvx_qmv_allgather(DUMMY, DUMMY, DUMMY, DUMMY, ctypes.byref(gg) if gg else None,
+                                   M, N, 512, 64, 4, None)
+    assert call(None) == 1
+    g.world = 9
+    assert call(g) == 1            # more ranks than QVX_MAX_RANKS
+    g.world, g.rank = 2, 2
+    assert call(g) == 1            # rank outside the world
+    g.rank = 1
+    g.row0 = 12
+    assert call(g) == 1            # rows past n_total
+    g.row0 = 8
+    g.signal[1] = None
+    assert call(g) == 1            # a peer buffer missing
+    g.signal[1] = 4096
+    assert call(g, M=9) == 1       # decode only
+    assert ctypes.sizeof(_lib.QvxGather) == 160  # 8 + 8 pointers, epoch, 5 ints (+4 padding)

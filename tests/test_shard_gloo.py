@@ -124,3 +124,29 @@ def test_shard_rows_rules():
         shard_rows(10, 4, 0)
     with pytest.raises(ValueError):
         shard_rows(8, 2, 2)
+
+
+def test_plan_gather_layout():
+    from qvex.shard import plan_gather_layout
+    offs, total = plan_gather_layout([2 * 1024, 300, 16])
+    assert offs[0] == 256                      # 3 signal words, padded
+    assert all(o % 256 == 0 for o in offs)
+    assert offs[1] == offs[0] + 2048 and offs[2] == offs[1] + 512
+    assert total == offs[2] + 256
+    with pytest.raises(ValueError):
+        plan_gather_layout([0])
+
+
+def test_gather_descriptor_addresses():
+    """Signal words lead each rank's buffer and are indexed by slot in the kernel, so the
+    descriptor carries the buffer base, never base + slot (which would shift slot s to
+    word 2s and, past the padding, into the first output region)."""
+    from qvex.shard import gather_descriptor, plan_gather_layout
+    offs, _ = plan_gather_layout([2 * 4096] * 150)
+    bases = [1 << 40, 2 << 40]
+    for slot in (0, 97, 149):
+        d = gather_descriptor(bases, offs[slot], 12345 << 8, 1, slot, 8192, 4096)
+        assert [d.signal[r] for r in range(2)] == bases
+        assert [d.out[r] for r in range(2)] == [b + offs[slot] for b in bases]
+        assert d.epoch == 12345 << 8 and d.slot == slot and d.world == 2 and d.rank == 1
+        assert 4 * slot < offs[0]  # the kernel's signal word for this slot precedes every region
