@@ -12,10 +12,10 @@ above the 126 MB L2, so no flush is needed between steps.
 
 With --gpus N (torchrun, one rank per GPU) each projection is column-sharded: rank r
 owns a contiguous 1/N of the output rows (weights, scales, biases), and the shards are
-all-gathered after each projection (strong scaling: total work fixed): over NCCL by
-default, or with --gather fused inside the qmv kernel (qvx_qmv_allgather: every rank
-stores its rows into every rank's output buffer over NVLink and signals; no NCCL call
-inside the step).
+all-gathered after each projection (strong scaling: total work fixed).  By default the
+all-gather is fused into the qmv kernel (qvx_qmv_allgather: every rank stores its rows
+into every rank's output buffer over NVLink and signals; no NCCL call inside the step);
+--gather nccl runs the local kernel followed by an NCCL all-gather instead.
 
 Prints ONE JSON line (rank 0).  `--impl reference` times the reference's arithmetic on
 the host CPU cores instead (the oracle port of engine/kernels.py's qmv arithmetic: MLX,
@@ -50,7 +50,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=1, help="tokens per step (1 = batch-1 decode)")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers (32 = the full 9B shape)")
-    ap.add_argument("--gather", choices=("fused", "nccl"), default="nccl",
+    ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
                     help="N>1: all-gather fused into the qmv kernel (peer stores over NVLink) or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the M=2/4/8 side measurements")

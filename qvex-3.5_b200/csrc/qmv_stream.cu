@@ -83,9 +83,12 @@ struct QmvGather {
   int world, rank, n_total, row0, slot;
 };
 
-__device__ __forceinline__ void red_add_release_sys(unsigned* addr, unsigned v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+// Relaxed: the fence before it orders the data.  (A release form carries its own
+// system-scope fence: measured on B200 at ~3.5 us per signal, on top of the explicit one.)
+__device__ __forceinline__ void red_add_relaxed_sys(unsigned* addr, unsigned v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
   unsigned v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
@@ -339,10 +342,11 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
         for (int q = 0; q < g.world; ++q)
           if (q != g.rank) copy_bf16_segment(g.out[q] + at, g.out[g.rank] + at, nrows, lane);
       }
-      __threadfence_system();
+      // every lane's peer stores are ordered before the signals by its own fence
+      fence_acq_rel_sys();
       __syncwarp();
       if (lane == 0)
-        for (int q = 0; q < g.world; ++q) red_add_release_sys(g.signal[q] + g.slot, 1u);
+        for (int q = 0; q < g.world; ++q) red_add_relaxed_sys(g.signal[q] + g.slot, 1u);
     }
   }
   __syncthreads();
