@@ -162,6 +162,15 @@ int qvx_dequantize_rows(const uint32_t* wq, const void* scales, const void* bias
 
 /* ---------------------------------------------------------------- gated DeltaNet */
 
+/* The q/k conditioning in front of gated_delta (engine/model.py:275-277):
+ *   q_out = Dk^-1 * rms_norm(q),  k_out = Dk^-1/2 * rms_norm(k)   (no weight, eps 1e-6)
+ * over `rows` bf16 rows of length D of each of q and k (rows = B*T*Hk, D = Dk).  fp32
+ * statistics; rms_norm's result and the product are each rounded to bf16, and the factors
+ * are the bf16 values of the reference's Python floats.  D even, 2..256; pointers 4-byte
+ * aligned; q_out / k_out may alias q / k. */
+int qvx_qk_condition(const void* q, const void* k, void* q_out, void* k_out, long long rows,
+                     int D, void* stream);
+
 /* Replaces gated_delta(q, k, v, a, b, A_log, dt_bias, state, keep_mid)
  * (engine/kernels.py:92-116).
  *   q, k      bf16 [B, T, Hk, Dk]      v  bf16 [B, T, Hv, Dv]

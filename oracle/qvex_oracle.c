@@ -338,7 +338,11 @@ int orc_gated_delta(const uint16_t* q, const uint16_t* k, const uint16_t* v, con
 
 /* q,k bf16 [rows, D] in place: q <- D^-1 rms_norm(q), k <- D^-1/2 rms_norm(k). */
 void orc_qk_condition(uint16_t* q, uint16_t* k, int64_t rows, int D) {
-  const float inv = 1.0f / sqrtf((float)D);
+  /* engine/model.py:275: inv = self.dk ** -0.5 is a Python float; MLX gives a Python
+   * scalar the dtype of the array it multiplies, so the factors are bf16(inv*inv) and
+   * bf16(inv) (1/128 and 0.08837890625 at Dk = 128) */
+  const double inv = 1.0 / sqrt((double)D);
+  const float sc_q = bf2f(f2bf((float)(inv * inv))), sc_k = bf2f(f2bf((float)inv));
   for (int64_t r = 0; r < rows; ++r) {
     for (int which = 0; which < 2; ++which) {
       uint16_t* p = (which == 0 ? q : k) + r * D;
@@ -348,7 +352,7 @@ void orc_qk_condition(uint16_t* q, uint16_t* k, int64_t rows, int D) {
         ss += f * f;
       }
       const float rn = 1.0f / sqrtf(ss / (float)D + 1e-6f);
-      const float sc = which == 0 ? inv * inv : inv;
+      const float sc = which == 0 ? sc_q : sc_k;
       /* rms_norm rounds to the input dtype, then the scalar product rounds again */
       for (int i = 0; i < D; ++i) p[i] = f2bf(sc * bf2f(f2bf(bf2f(p[i]) * rn)));
     }

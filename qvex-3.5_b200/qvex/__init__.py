@@ -2,19 +2,19 @@
 
 Public surface (mirrors the reference's):
   quantized_matmul, quantize, dequantize   -- mx.quantized_matmul / mx.quantize / mx.dequantize
-  gated_delta, qmv_multi                   -- engine/kernels.py
+  gated_delta, qmv_multi, qk_condition     -- engine/kernels.py, engine/model.py:275-277
   QLinear, QEmbedding, RecurrentCache      -- engine/model.py
   shard                                    -- column sharding over GPUs with an all-gather
 All compute runs in libqvex.so (C ABI, include/qvex.h) through ctypes.
 """
 from .core import dequantize, dequantize_rows, qmm_workspace_size, quantize, quantized_matmul
-from .kernels import gated_delta, qmv_multi
+from .kernels import gated_delta, qk_condition, qmv_multi
 from .model import QEmbedding, QLinear, RecurrentCache
 from ._lib import QvexError, QvexTimeout, lib as _load_lib
 
 __all__ = [
     "quantized_matmul", "quantize", "dequantize", "dequantize_rows", "qmm_workspace_size",
-    "gated_delta", "qmv_multi", "QLinear", "QEmbedding", "RecurrentCache", "QvexError", "QvexTimeout",
+    "gated_delta", "qk_condition", "qmv_multi", "QLinear", "QEmbedding", "RecurrentCache", "QvexError", "QvexTimeout",
     "load_library",
 ]
 

@@ -39,6 +39,7 @@ SIGNATURES = {
     "qvx_dequantize": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "qvx_dequantize_rows": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "qvx_gated_delta": (_I, [_P] * 11 + [_I] * 6 + [_P]),
+    "qvx_qk_condition": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, _P]),
 }
 
 

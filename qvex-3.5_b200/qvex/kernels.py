@@ -51,6 +51,21 @@ def gated_delta(q, k, v, a, b, A_log, dt_bias, state, keep_mid: bool = False, *,
     return (y, out_state, mid) if keep_mid else (y, out_state)
 
 
+def qk_condition(q, k):
+    """q, k [..., Dk] bf16 -> (Dk^-1 * rms_norm(q), Dk^-1/2 * rms_norm(k)), the conditioning
+    GatedDeltaNet applies before gated_delta (engine/model.py:275-277).  New tensors."""
+    _require_cuda("q", q, (torch.bfloat16,))
+    _require_cuda("k", k, (torch.bfloat16,))
+    if q.shape != k.shape:
+        raise ValueError("q and k must have the same shape")
+    D = q.shape[-1]
+    q, k = q.contiguous(), k.contiguous()
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    check(lib().qvx_qk_condition(_ptr(q), _ptr(k), _ptr(qo), _ptr(ko), q.numel() // D, D, _stream(q)),
+          "qvx_qk_condition")
+    return qo, ko
+
+
 def qmv_multi(x, w, scales, biases):
     """x [M, K] (M small), w [N, K/8] uint32 4-bit/group-64 -> y [M, N]"""
     if x.dim() != 2:

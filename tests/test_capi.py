@@ -142,3 +142,11 @@ def test_qmv_allgather_rejects_bad_descriptors(L):
     g.signal[1] = 4096
     assert call(g, M=9) == 1       # decode only
     assert ctypes.sizeof(_lib.QvxGather) == 160  # 8 + 8 pointers, epoch, 5 ints (+4 padding)
+
+
+def test_qk_condition_rejects(L):
+    assert L.qvx_qk_condition(DUMMY, DUMMY, DUMMY, DUMMY, 8, 127, None) == 1   # odd D
+    assert L.qvx_qk_condition(DUMMY, DUMMY, DUMMY, DUMMY, 8, 258, None) == 1   # D > 256
+    assert L.qvx_qk_condition(DUMMY, DUMMY, DUMMY, DUMMY, -1, 128, None) == 1
+    assert L.qvx_qk_condition(P(4098), DUMMY, DUMMY, DUMMY, 8, 128, None) == 3
+    assert L.qvx_qk_condition(None, None, None, None, 0, 128, None) == 0       # nothing to do

@@ -177,6 +177,34 @@ def test_dequantize_rows_bad_id_sets_device_status(qvex):
 
 # ------------------------------------------------------------------ gated DeltaNet
 
+@pytest.mark.parametrize("shape", [(1, 64, 16, 128), (2, 3, 16, 128), (1, 5, 4, 64), (3, 1, 7, 32), (1, 2, 3, 256)])
+def test_qk_condition_bit_exact(qvex, shape):
+    """engine/model.py:275-277 conditioning: bit-exact with the oracle (same fp32 sum order
+    and the same two bf16 roundings); row counts that do not fill a 128-row block."""
+    q = O.f32_to_bf16(detrand.normal(shape, 61) * 3.0)
+    k = O.f32_to_bf16(detrand.normal(shape, 62) * 0.01)
+    rq, rk = O.qk_condition(q, k)
+    gq, gk = qvex.qk_condition(dev(q), dev(k))
+    torch.cuda.synchronize()
+    assert np.array_equal(host_u16(gq), rq) and np.array_equal(host_u16(gk), rk)
+
+
+def test_qk_condition_in_place_and_zero_rows(qvex):
+    import ctypes
+    from qvex import _lib
+    q = O.f32_to_bf16(detrand.normal((300, 128), 63))
+    k = O.f32_to_bf16(detrand.normal((300, 128), 64))
+    rq, rk = O.qk_condition(q, k)
+    qd, kd = dev(q), dev(k)
+    P = ctypes.c_void_p
+    s = P(torch.cuda.current_stream().cuda_stream)
+    _lib.check(_lib.lib().qvx_qk_condition(P(qd.data_ptr()), P(kd.data_ptr()), P(qd.data_ptr()),
+                                           P(kd.data_ptr()), 300, 128, s), "qk")
+    assert _lib.lib().qvx_qk_condition(P(qd.data_ptr()), P(kd.data_ptr()), P(qd.data_ptr()),
+                                       P(kd.data_ptr()), 0, 128, s) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(host_u16(qd), rq) and np.array_equal(host_u16(kd), rk)
+
 def run_gd(qvex, q, k, v, a, b, A_log, dt, st, keep_mid):
     outs = qvex.gated_delta(dev(q), dev(k), dev(v), dev(a), dev(b), torch.from_numpy(A_log).cuda(),
                             torch.from_numpy(dt).cuda(), torch.from_numpy(st).cuda(), keep_mid=keep_mid)
