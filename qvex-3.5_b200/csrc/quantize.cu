@@ -2,11 +2,11 @@
 //
 // quantize replaces mx.quantize(w, group_size=64, bits=4) (tools/fetch_mtp.py:99,
 // bench/qmv_kernel_bench.py:14) with the packing order of quant/quantize.py:71-75:
-// element k of a row sits in word k/8 at bits 4*(k%8).  Eight lanes own one 64-group
-// (8 bf16 = one 16-byte load each); min/max meet through 3 shuffles; each lane packs
-// its 8 codes into one word, so a group writes 32 contiguous bytes.  All arithmetic is
-// IEEE fp32 with round-to-nearest (explicit __fsub_rn/__fdiv_rn, rint), which makes the
-// codes and the bf16 scales/biases bit-exact with the CPU restatement.
+// element k of a row sits in word k/8 at bits 4*(k%8).  One thread owns one 64-group
+// (8 x 16-byte loads, 32 contiguous bytes of codes out).  The group fit is IEEE fp32 with
+// round-to-nearest (__fsub_rn/__fdiv_rn, rint) and the codes equal rint(RN((w-b)/s))
+// exactly (reciprocal with an exact fallback, see code_of), which makes the codes and the
+// bf16 scales/biases bit-exact with the CPU restatement.
 //
 // dequantize (mx.dequantize, engine/model.py:127) writes bf16(fma(s, q, b)), one word
 // (8 values, one 16-byte store) per thread.  dequantize_rows is the QEmbedding gather
@@ -40,51 +40,83 @@ __device__ __forceinline__ void group_params(float mn, float mx, int variant, fl
   }
 }
 
-// One thread = 8 consecutive weights (one packed word); 8 threads = one group.
+// One thread = one 64-group (128 bytes of w in, 32 bytes of codes out): min/max and the 64
+// codes are independent work inside the thread, with no shuffles between lanes.
+//
+// Codes without a division per element.  The reference code is c = rint(RN(t / s)) with
+// t = RN(w - b).  With r = RN(1/s) (one IEEE division per group) and y = RN(t * r),
+// |y - t/s| <= |t/s| * 2^-23 (two roundings) and |RN(t/s) - t/s| <= |t/s| * 2^-24, so
+// |y - RN(t/s)| <= 1.5 * 2^-23 * |y| (to first order).  When y lies farther than
+// |y| * 2^-20 from every half-integer, y and RN(t/s) fall in the same interval between
+// half-integers and rint gives the same integer; only in that rare band is the IEEE
+// quotient computed.  NaN and infinite inputs give the same codes on both paths (NaN
+// clamps to 0; the scale is never 0).
+__device__ __forceinline__ uint32_t code_of(float v, float bias, float scale, float recip) {
+  const float t = __fsub_rn(v, bias);
+  const float y = __fmul_rn(t, recip);
+  float c = rintf(y);
+  const float half_gap = 0.5f - fabsf(__fsub_rn(y, c));  // distance to the nearest half-integer
+  if (half_gap <= fabsf(y) * 0x1p-20f) c = rintf(__fdiv_rn(t, scale));
+  return (uint32_t)fminf(fmaxf(c, 0.0f), 15.0f);
+}
+
 __global__ void __launch_bounds__(256) quantize_kernel(const uint4* __restrict__ w, uint32_t* __restrict__ wq,
                                                        __nv_bfloat16* __restrict__ scales,
-                                                       __nv_bfloat16* __restrict__ biases, long long nwords,
-                                                       int variant) {
+                                                       __nv_bfloat16* __restrict__ biases, long long ngroups,
+                                                       int variant, bool wq16) {
   const long long stride = (long long)gridDim.x * blockDim.x;
-  // the loop trip count is uniform across each 8-lane group (nwords % 8 == 0)
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i - (threadIdx.x & 31) < nwords;
-       i += stride) {
-    const bool live = i < nwords;
-    const uint4 t = live ? ld_stream_v4(w + i) : make_uint4(0, 0, 0, 0);
-    const uint32_t u[4] = {t.x, t.y, t.z, t.w};
-    float v[8];
+  for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < ngroups; g += stride) {
+    // 8 x 16 B of one group: the lines stay in L1 between the loads of one thread
+    uint4 t[8];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      v[2 * h] = __uint_as_float(u[h] << 16);
-      v[2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
-    }
-    float mn = v[0], mx = v[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) {
-      mn = fminf(mn, v[j]);
-      mx = fmaxf(mx, v[j]);
-    }
-#pragma unroll
-    for (int off = 1; off < 8; off <<= 1) {
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    }
-    float scale, bias;
-    group_params(mn, mx, variant, &scale, &bias);
-    uint32_t word = 0;
+    for (int j = 0; j < 8; ++j) t[j] = __ldg(w + g * 8 + j);
+    // min / max as a tree (6 levels instead of a 64-long dependent chain)
+    float pmn[8], pmx[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float c = rintf(__fdiv_rn(__fsub_rn(v[j], bias), scale));
-      c = fminf(fmaxf(c, 0.0f), 15.0f);
-      word |= (uint32_t)c << (4 * j);
-    }
-    if (live) {
-      wq[i] = word;
-      if ((threadIdx.x & 7) == 0) {
-        scales[i >> 3] = __float2bfloat16_rn(scale);
-        biases[i >> 3] = __float2bfloat16_rn(bias);
+      const uint32_t u[4] = {t[j].x, t[j].y, t[j].z, t[j].w};
+      float a[4], b[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float lo = __uint_as_float(u[h] << 16), hi = __uint_as_float(u[h] & 0xffff0000u);
+        a[h] = fminf(lo, hi);
+        b[h] = fmaxf(lo, hi);
       }
+      pmn[j] = fminf(fminf(a[0], a[1]), fminf(a[2], a[3]));
+      pmx[j] = fmaxf(fmaxf(b[0], b[1]), fmaxf(b[2], b[3]));
     }
+#pragma unroll
+    for (int w2 = 4; w2 > 0; w2 >>= 1)
+#pragma unroll
+      for (int j = 0; j < w2; ++j) {
+        pmn[j] = fminf(pmn[j], pmn[j + w2]);
+        pmx[j] = fmaxf(pmx[j], pmx[j + w2]);
+      }
+    float scale, bias;
+    group_params(pmn[0], pmx[0], variant, &scale, &bias);
+    const float recip = __fdiv_rn(1.0f, scale);
+    uint32_t word[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t u[4] = {t[j].x, t[j].y, t[j].z, t[j].w};
+      uint32_t wd = 0;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        wd |= code_of(__uint_as_float(u[h] << 16), bias, scale, recip) << (8 * h);
+        wd |= code_of(__uint_as_float(u[h] & 0xffff0000u), bias, scale, recip) << (8 * h + 4);
+      }
+      word[j] = wd;
+    }
+    if (wq16) {  // the usual case: two 16-byte stores
+      uint4* o = reinterpret_cast<uint4*>(wq + g * 8);
+      o[0] = make_uint4(word[0], word[1], word[2], word[3]);
+      o[1] = make_uint4(word[4], word[5], word[6], word[7]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wq[g * 8 + j] = word[j];
+    }
+    scales[g] = __float2bfloat16_rn(scale);
+    biases[g] = __float2bfloat16_rn(bias);
   }
 }
 
@@ -153,10 +185,10 @@ extern "C" int qvx_quantize(const void* w, uint32_t* wq, void* scales, void* bia
   if (!w || !wq || !scales || !biases) return fail(QVX_ERR_INVALID, "qvx_quantize: null pointer");
   if (!aligned(w, 16) || !aligned(wq, 4) || !aligned(scales, 2) || !aligned(biases, 2))
     return fail(QVX_ERR_ALIGN, "qvx_quantize: w must be 16-byte aligned");
-  const long long nwords = (long long)N * (K / 8);
-  quantize_kernel<<<grid_for(nwords, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  const long long ngroups = (long long)N * (K / 64);
+  quantize_kernel<<<grid_for(ngroups, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(w), wq, static_cast<__nv_bfloat16*>(scales), static_cast<__nv_bfloat16*>(biases),
-      nwords, variant);
+      ngroups, variant, aligned(wq, 16));
   return check_launch("qvx_quantize");
 }
 
