@@ -16,7 +16,7 @@
 // time share weight rows in L2 while x stays L2-resident.
 //
 // One ring of S stages, each holding the stage's x tile (2 x 16 KB), code tile (16 KB)
-// and group multipliers (4 KB), filled by TMA (full[s]) and released by ONE tcgen05
+// and group multipliers (4 KB), filled by TMA (full[]) and released by ONE tcgen05
 // commit of the MMA thread (empty[s]) -- the dequantisers have read the codes before the
 // MMAs that release the stage could start.  The dequantised A tile has two tensor-memory
 // stages; step L writes stage L % 2, which is free once the MMAs of step L - 2 are done,
@@ -56,6 +56,15 @@ constexpr int BM = 256;  // weight rows per tile
 constexpr int BN = 128;  // tokens per tile (MMA N)
 constexpr int BK = 128;  // K per stage (two groups)
 constexpr int S = 3;     // ring stages (shared memory)
+// "Data of step L landed" barriers: 2S of them, step L using full[L % (2S)].  A wait on a
+// barrier names only the parity of the phase it wants, and one still in the phase before
+// reads as complete for the next.  With one barrier per ring slot, a dequant group could
+// reach step L while the other group's step L - 3 (same slot, the phase before) had not
+// landed -- copies land out of order when a whole ring is issued at once -- and dequantise
+// step L - 3's codes; that was seen on B200.  With 2S barriers the phase before belongs to
+// step L - 6, which this group's own A-free wait at step L - 2 (the MMAs of step L - 4
+// are done) has already shown to have landed.
+constexpr int NFULL = 2 * S;
 constexpr int DQ_GROUPS = 2;
 constexpr int DQ_WARPS_PER_GROUP = 8;  // 2 halves x 4 lane quarters
 constexpr int NUM_DQ_WARPS = DQ_GROUPS * DQ_WARPS_PER_GROUP;
@@ -79,7 +88,7 @@ constexpr uint32_t OFF_PRM = X_BYTES + CODE_BYTES;
 constexpr uint32_t OFF_EPI = S * STAGE_BYTES;  // bf16 output tile [BN][BM] for the TMA store
 constexpr uint32_t EPI_BYTES = BN * BM * 2;    // 64 KB
 constexpr uint32_t OFF_BAR = OFF_EPI + EPI_BYTES;
-constexpr uint32_t NUM_BARS = 2 * S + DQ_GROUPS + 5;
+constexpr uint32_t NUM_BARS = NFULL + S + DQ_GROUPS + 5;
 constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
@@ -129,7 +138,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* full = bars;
-  uint64_t* empty = full + S;
+  uint64_t* empty = full + NFULL;
   uint64_t* full_a = empty + S;
   uint64_t* acc_full = full_a + DQ_GROUPS;
   uint64_t* acc_empty = acc_full + 1;
@@ -148,10 +157,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int total = my_tiles * nks;  // stages this CTA runs
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
+    for (int i = 0; i < NFULL; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < S; ++i) mbar_init(&empty[i], 1);
     for (int i = 0; i < DQ_GROUPS; ++i) mbar_init(&full_a[i], DQ_WARPS_PER_GROUP);
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
@@ -179,7 +186,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     for (int L = group; L < total && ok; L += DQ_GROUPS) {
       const int s = L % S;
-      if (!(ok = mbar_wait(&full[s], (uint32_t)(L / S) & 1u, abort_flag, status))) break;
+      if (!(ok = mbar_wait(&full[L % NFULL], (uint32_t)(L / NFULL) & 1u, abort_flag, status))) break;
       const uint8_t* st = smem + s * STAGE_BYTES;
       const uint8_t* crow = st + OFF_CODE + r * 64;
       const uint4 c0 = *reinterpret_cast<const uint4*>(crow + ((0u ^ swz) << 4));
@@ -308,15 +315,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int s = it % S;
           if (!(ok = mbar_wait(&empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, abort_flag, status))) break;
           uint8_t* st = smem + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          tma_tile_2d_g2s(smem_u32(st), &tmap_x, &full[s], ks * BK, m_base);
-          tma_tile_2d_g2s(smem_u32(st + X_HALF_BYTES), &tmap_x, &full[s], ks * BK + 64, m_base);
-          tma_tile_2d_g2s(smem_u32(st + OFF_CODE), &tmap_w, &full[s], ks * (BK / 8), n_base);
-          tma_bulk_g2s(st + OFF_PRM, prm + ((size_t)ks * n_pad + n_base) * 2, PRM_BYTES, &full[s]);
+          uint64_t* fb = &full[it % NFULL];
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          tma_tile_2d_g2s(smem_u32(st), &tmap_x, fb, ks * BK, m_base);
+          tma_tile_2d_g2s(smem_u32(st + X_HALF_BYTES), &tmap_x, fb, ks * BK + 64, m_base);
+          tma_tile_2d_g2s(smem_u32(st + OFF_CODE), &tmap_w, fb, ks * (BK / 8), n_base);
+          tma_bulk_g2s(st + OFF_PRM, prm + ((size_t)ks * n_pad + n_base) * 2, PRM_BYTES, fb);
         }
       }
       // let the copies already issued land before the CTA can exit
-      for (int j = max(0, it - S); j < it; ++j) mbar_wait_drain(&full[j % S], (uint32_t)(j / S) & 1u, status);
+      for (int j = max(0, it - S); j < it; ++j)
+        mbar_wait_drain(&full[j % NFULL], (uint32_t)(j / NFULL) & 1u, status);
     }
   } else {
     // ------------------------------------------------------------ MMA issuer
@@ -327,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // tensor cores are still working through the queued MMAs while this thread polls,
       // instead of idling for the ~300 cycles two barrier waits take.
       auto wait_stage = [&](int i) {
-        return mbar_wait(&full[i % S], (uint32_t)(i / S) & 1u, abort_flag, status) &&
+        return mbar_wait(&full[i % NFULL], (uint32_t)(i / NFULL) & 1u, abort_flag, status) &&
                mbar_wait(&full_a[i % DQ_GROUPS], (uint32_t)(i / DQ_GROUPS) & 1u, abort_flag, status);
       };
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
