@@ -5,12 +5,13 @@
 // that bytes in flight do not cost registers and consecutive launches overlap:
 //
 //   * warp W-2 (producer) streams blocks of R whole rows -- codes (R*K/2 contiguous
-//     bytes), scales and biases (R*K/32 bytes each) -- into an 8-stage shared-memory ring
-//     with cp.async.bulk, completion counted on an mbarrier.  It runs before
-//     griddepcontrol.wait: weights do not depend on the upstream kernel.
-//   * one CTA per SM using under half of the SM, so with programmatic dependent launch the
-//     NEXT projection's CTA is already resident and its producer fills its own ring while
-//     this one computes: HBM stays busy across launch boundaries.
+//     bytes), scales and biases (R*K/32 bytes each) -- into a shared-memory ring of 4-9
+//     stages (up to ~200 KB in flight per SM) with cp.async.bulk, completion counted on an
+//     mbarrier.  It runs before griddepcontrol.wait: weights do not depend on the upstream
+//     kernel, so under programmatic dependent launch each SM's next CTA starts streaming as
+//     soon as the previous one leaves.
+//   * one CTA per SM; without a gather, CTA b takes row blocks b, b + grid, ..., so the grid
+//     sweeps the weights front to back like a copy kernel.
 //   * compute warps form T teams of P = K/1024 warps; team t owns rows t*RT..t*RT+RT-1 of
 //     every stage, and lane l of warp p of a team owns the 32 inputs
 //     [1024p + 32l, +32) of K (one conflict-free LDS.128 of codes per row).
@@ -30,6 +31,7 @@
 //     sum q * p_j in int32 (no overflow: 15*255*32 < 2^17);
 //   * per row: Q = a0 + 256 a1 + 65536 a2, sum(q x) = 2^(E-22) Q, and the group term of the
 //     reference factorisation s*sum(q x) + b*sum(x) (engine/kernels.py:151-171).
+//   * at M >= 2 (two tokens per CTA) x takes two planes, 14-bit fixed point, instead.
 #include <cstring>
 
 #include "sm100.cuh"
@@ -37,9 +39,10 @@
 namespace qvx {
 
 constexpr int kStreamMaxComputeWarps = 12;
-// Shared memory per CTA: kept under half of the SM (228 KB, 1 KB of it reserved per CTA)
-// so that two launches are co-resident.
-constexpr size_t kStreamSmemBudget = 112 * 1024;
+// Shared memory per CTA.  Measured on B200 over the 145 launches of a decode step: a
+// 200 KB ring (one CTA per SM, 9 stages of ~20 KB at K = 4096) streams 3.4% faster than a
+// 112 KB ring that lets two consecutive launches share an SM.
+constexpr size_t kStreamSmemBudget = 200 * 1024;
 // Codes per stage: measured on B200, 16 KB stages (4 rows per team at K = 4096) stream
 // lm_head at ~80% of HBM against ~63% for 8 KB stages.
 constexpr size_t kStreamStageCodeBytes = 16384;
@@ -121,24 +124,39 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 
 // x planes of one token for a lane's 32 inputs: pl[j][2*w + h] packs, for packed word w
 // (inputs 8w..8w+7), the plane-j bytes of inputs 8w+h, 8w+h+2, 8w+h+4, 8w+h+6.
+// PL = 3: 22-bit fixed point (one token per CTA; exact for every bf16 input within 2^14 of
+// the slice max).  PL = 2: 14-bit fixed point (two tokens per CTA, where the dp4a issue
+// rate bounds the kernel: four DP4As per 8 codes and token instead of six, measured 17-19%
+// faster at M = 2..8; error <= 2^-15 of the slice max per input, ~1e-5 relative on y).
+template <int PL>
 struct XPlanes {
-  uint32_t pl[3][8];
-  float scale;  // 2^(E-23)
+  uint32_t pl[PL][8];
+  float scale;  // 2^(E-FB)
   float xsum;   // sum of the 32 inputs
 };
 
-__device__ __forceinline__ void make_planes(const float (&xf)[32], XPlanes& xp) {
+template <int PL>
+__device__ __forceinline__ float bf16_at(const uint32_t (&u)[16], int i) {
+  return __uint_as_float((i & 1) ? (u[i >> 1] & 0xffff0000u) : (u[i >> 1] << 16));
+}
+
+// u: the lane's 32 bf16 inputs as 16 raw words (input i in the low half of word i/2 when i
+// is even, the high half when odd)
+template <int PL>
+__device__ __forceinline__ void make_planes(const uint32_t (&u)[16], XPlanes<PL>& xp) {
+  constexpr int FB = PL == 3 ? 22 : 14;  // fraction bits against the slice max
   float mx = 0.0f, sum = 0.0f;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    mx = fmaxf(mx, fabsf(xf[i]));
-    sum += xf[i];
+    const float v = bf16_at<PL>(u, i);
+    mx = fmaxf(mx, fabsf(v));
+    sum += v;
   }
   int E = 0;
   if (mx > 0.0f && isfinite(mx)) frexpf(mx, &E);  // 2^(E-1) <= mx < 2^E
   E = max(E, -100);                                // E <= 128, so both powers below are normal
-  const float up = __int_as_float((22 - E + 127) << 23);   // 2^(22-E)
-  xp.scale = __int_as_float((E - 22 + 127) << 23);         // 2^(E-22)
+  const float up = __int_as_float((FB - E + 127) << 23);   // 2^(FB-E)
+  xp.scale = __int_as_float((E - FB + 127) << 23);         // 2^(E-FB)
   xp.xsum = sum;
 #pragma unroll
   for (int w = 0; w < 4; ++w)
@@ -147,12 +165,13 @@ __device__ __forceinline__ void make_planes(const float (&xf)[32], XPlanes& xp) 
       uint32_t v[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        // x * 2^(22-E) has |.| < 2^22, so adding 1.5 * 2^23 lands in [2^23, 2^24) where the
-        // float spacing is 1: one FFMA rounds to the nearest integer, exactly
-        v[i] = (uint32_t)(__float_as_int(fmaf(xf[8 * w + h + 2 * i], up, 12582912.0f)) - 0x4B400000);
-      // byte j of the four values -> plane j, three PRMTs per plane
+        // x * 2^(FB-E) has |.| < 2^FB <= 2^22, so adding 1.5 * 2^23 lands in [2^23, 2^24)
+        // where the float spacing is 1: one FFMA rounds to the nearest integer, exactly
+        v[i] = (uint32_t)(__float_as_int(fmaf(bf16_at<PL>(u, 8 * w + h + 2 * i), up, 12582912.0f)) - 0x4B400000);
+      // byte j of the four values -> plane j, three PRMTs per plane; the top plane is
+      // signed (|x_fix| <= 2^FB, so it fits a byte)
 #pragma unroll
-      for (int j = 0; j < 3; ++j) {
+      for (int j = 0; j < PL; ++j) {
         const uint32_t sel = 0x0040u + 0x0011u * (uint32_t)j;  // (v_a byte j, v_b byte j)
         xp.pl[j][2 * w + h] = __byte_perm(__byte_perm(v[0], v[1], sel), __byte_perm(v[2], v[3], sel), 0x5410);
       }
@@ -166,6 +185,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
                       int M, int N, int K, int T, int* status, const QmvGather g) {
   using VC = VCfg<RT * MC>;
   constexpr int V = VC::V, LV = VC::LV;
+  constexpr int PL = MC == 1 ? 3 : 2;  // x planes (see XPlanes)
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int NW = blockDim.x >> 5;          // warps
@@ -182,11 +202,17 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
 
   const int m0 = blockIdx.y * MC;
   const int mc = min(MC, M - m0);
-  const int r_begin = (int)(((long long)blockIdx.x * N) / gridDim.x);
-  const int r_end = (int)(((long long)(blockIdx.x + 1) * N) / gridDim.x);
-  const int nchunks = (r_end - r_begin + R - 1) / R;
-
   const bool gather = g.world > 0;
+  // Row chunks of R rows.  Without a gather, CTA b takes chunks b, b + grid, b + 2 grid, ...,
+  // so that at any moment the grid streams one contiguous stretch of the weights (measured
+  // faster than one contiguous range per CTA).  A gathering launch keeps one contiguous
+  // range per CTA, which it copies to the peers in one piece at the end.
+  const int r_begin = gather ? (int)(((long long)blockIdx.x * N) / gridDim.x) : 0;
+  const int r_end = gather ? (int)(((long long)(blockIdx.x + 1) * N) / gridDim.x) : N;
+  const int nchunks = gather ? (r_end - r_begin + R - 1) / R
+                             : ((N + R - 1) / R - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  auto chunk_row = [&](int c) { return gather ? r_begin + c * R : ((int)blockIdx.x + c * (int)gridDim.x) * R; };
+
   // thread 0 is a compute thread, so it has passed griddepcontrol.wait before it waits here
   const bool gather_waiter = gather && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0;
   if (threadIdx.x == 0) {
@@ -211,7 +237,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
         const int s = c % S;
         const uint32_t ph = (uint32_t)(c / S) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status)) break;
-        const int r0 = r_begin + c * R;
+        const int r0 = chunk_row(c);
         const int nr = min(R, r_end - r0);
         const uint32_t cb = (uint32_t)nr * (uint32_t)K / 2u, sb = (uint32_t)nr * (uint32_t)G * 2u;
         uint8_t* st = stage(s);
@@ -230,23 +256,18 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     const bool kact = FULLK || k0 < K;
     const int g = kact ? (k0 >> 6) : 0;
     pdl_wait();  // x comes from the upstream kernel
-    XPlanes xp[MC];
+    XPlanes<PL> xp[MC];
 #pragma unroll
     for (int m = 0; m < MC; ++m) {
       const bool live = kact && m < mc;
       const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(m0 + (live ? m : 0)) * K + (live ? k0 : 0));
-      float xf[32];
+      uint32_t u[16];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint4 t = live ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
-        const uint32_t u[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          xf[c * 8 + 2 * h] = __uint_as_float(u[h] << 16);
-          xf[c * 8 + 2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
-        }
+        u[4 * c] = t.x; u[4 * c + 1] = t.y; u[4 * c + 2] = t.z; u[4 * c + 3] = t.w;
       }
-      make_planes(xf, xp[m]);
+      make_planes<PL>(u, xp[m]);
     }
     for (int c = 0; c < nchunks; ++c) {
       const int s_ = c % S;
@@ -275,23 +296,39 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
         }
 #pragma unroll
         for (int m = 0; m < MC; ++m) {
-          // six independent chains (plane x even/odd codes), four DP4As deep
-          uint32_t a0l = 0, a1l = 0, a0h = 0, a1h = 0;
-          int a2l = 0, a2h = 0;
+          float q;  // sum q * x_fix
+          if constexpr (PL == 3) {
+            // six independent chains (plane x even/odd codes), four DP4As deep
+            uint32_t a0l = 0, a1l = 0, a0h = 0, a1h = 0;
+            int a2l = 0, a2h = 0;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            a0l = dp4a_uu(lo[j], xp[m].pl[0][2 * j], a0l);
-            a1l = dp4a_uu(lo[j], xp[m].pl[1][2 * j], a1l);
-            a2l = dp4a_us(lo[j], xp[m].pl[2][2 * j], a2l);
-            a0h = dp4a_uu(hi[j], xp[m].pl[0][2 * j + 1], a0h);
-            a1h = dp4a_uu(hi[j], xp[m].pl[1][2 * j + 1], a1h);
-            a2h = dp4a_us(hi[j], xp[m].pl[2][2 * j + 1], a2h);
+            for (int j = 0; j < 4; ++j) {
+              a0l = dp4a_uu(lo[j], xp[m].pl[0][2 * j], a0l);
+              a1l = dp4a_uu(lo[j], xp[m].pl[1][2 * j], a1l);
+              a2l = dp4a_us(lo[j], xp[m].pl[2][2 * j], a2l);
+              a0h = dp4a_uu(hi[j], xp[m].pl[0][2 * j + 1], a0h);
+              a1h = dp4a_uu(hi[j], xp[m].pl[1][2 * j + 1], a1h);
+              a2h = dp4a_us(hi[j], xp[m].pl[2][2 * j + 1], a2h);
+            }
+            // |a| < 2^22: int -> float by the 1.5 * 2^23 magic number, exactly and off the XU pipe
+            const float f0 = __int_as_float(0x4B400000 + (int)(a0l + a0h)) - 12582912.0f;
+            const float f1 = __int_as_float(0x4B400000 + (int)(a1l + a1h)) - 12582912.0f;
+            const float f2 = __int_as_float(0x4B400000 + (a2l + a2h)) - 12582912.0f;
+            q = fmaf(f2, 65536.0f, fmaf(f1, 256.0f, f0));
+          } else {
+            uint32_t a0l = 0, a0h = 0;
+            int a1l = 0, a1h = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              a0l = dp4a_uu(lo[j], xp[m].pl[0][2 * j], a0l);
+              a1l = dp4a_us(lo[j], xp[m].pl[1][2 * j], a1l);
+              a0h = dp4a_uu(hi[j], xp[m].pl[0][2 * j + 1], a0h);
+              a1h = dp4a_us(hi[j], xp[m].pl[1][2 * j + 1], a1h);
+            }
+            const float f0 = __int_as_float(0x4B400000 + (int)(a0l + a0h)) - 12582912.0f;
+            const float f1 = __int_as_float(0x4B400000 + (a1l + a1h)) - 12582912.0f;
+            q = fmaf(f1, 256.0f, f0);  // exact: |q| < 2^22
           }
-          // |a| < 2^22: int -> float by the 1.5 * 2^23 magic number, exactly and off the XU pipe
-          const float f0 = __int_as_float(0x4B400000 + (int)(a0l + a0h)) - 12582912.0f;
-          const float f1 = __int_as_float(0x4B400000 + (int)(a1l + a1h)) - 12582912.0f;
-          const float f2 = __int_as_float(0x4B400000 + (a2l + a2h)) - 12582912.0f;
-          const float q = fmaf(f2, 65536.0f, fmaf(f1, 256.0f, f0));  // sum q * x_fix
           const float part = fmaf(sf * xp[m].scale, q, bf * xp[m].xsum);
           pv[i * MC + m] = FULLK ? part : (kact ? part : 0.0f);
         }
@@ -309,7 +346,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       const int s = c % S;
       const uint32_t ph = (uint32_t)(c / S) & 1u;
       if (!mbar_wait(&done[s], ph, abort_flag, status)) break;
-      const int r0 = r_begin + c * R;
+      const int r0 = chunk_row(c);
       const int nr = min(R, r_end - r0);
       const float* red = reinterpret_cast<const float*>(stage(s) + (size_t)R * K / 2 + (size_t)R * K / 16);
       for (int v = lane; v < R * MC; v += 32) {
@@ -390,7 +427,7 @@ static int launch_stream(int T, const void* x, const uint32_t* w, const void* s,
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int chunks = (M + MC - 1) / MC;
-  // one CTA per SM: the other half of the SM is left to the next launch
+  // one CTA per SM (per token chunk)
   long long ctas = num_sms() / chunks;
   const long long need = (N + R - 1) / R;
   if (ctas > need) ctas = need;
@@ -425,13 +462,13 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   const int P = (K + 1023) / 1024;
   const int T = P >= 8 ? 1 : 8 / P;  // about 8 compute warps
   // rows per team per stage: the most (4, 2 or 1) that keeps a stage's codes within 16 KB
+  const int mc = M == 1 ? 1 : 2;  // tokens per CTA (x costs 26 registers per token)
   int rt = 4;
   while (rt > 1 && (size_t)T * rt * K / 2 > kStreamStageCodeBytes) rt /= 2;
-  const int mc = M == 1 ? 1 : 2;  // x costs 24 registers per token
   const bool fullk = K % 1024 == 0;
-  // ring depth: as many stages (4..7) as the shared-memory budget holds
+  // ring depth: as many stages (4..9) as the shared-memory budget holds
   int depth = (int)((kStreamSmemBudget - 16) / (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)));
-  depth = depth < 4 ? 4 : depth > 7 ? 7 : depth;
+  depth = depth < 4 ? 4 : depth > 9 ? 9 : depth;
 #define QVX_STREAM_S(MC_, RT_, S_)                                                                          \
   if (depth == S_)                                                                                          \
     return fullk ? launch_stream<MC_, RT_, true, S_>(T, x, w, s, b, y, M, N, K, stream, status, g)             \
@@ -442,6 +479,8 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
     QVX_STREAM_S(MC_, RT_, 5)                                                                               \
     QVX_STREAM_S(MC_, RT_, 6)                                                                               \
     QVX_STREAM_S(MC_, RT_, 7)                                                                               \
+    QVX_STREAM_S(MC_, RT_, 8)                                                                               \
+    QVX_STREAM_S(MC_, RT_, 9)                                                                               \
   }
   QVX_STREAM_CASE(1, 4)
   QVX_STREAM_CASE(1, 2)

@@ -67,6 +67,21 @@ def test_qmv_matches_oracle(qvex, M, N, K):
     assert rel_l2(host_u16(y), ref) <= MATMUL_TOL
 
 
+@pytest.mark.parametrize("M", [1, 2, 3, 8])
+def test_qmv_wide_dynamic_range(qvex, M):
+    """x spanning twelve decades inside each 32-input slice: the fixed-point planes are
+    scaled to the slice max, so small inputs lose bits, but the error stays a fraction of
+    the slice max and y stays within tolerance (M >= 3 uses 14-bit planes)."""
+    N, K = 1000, 4096
+    x, _, w, s, b = qmv_inputs(M, K, N, seed=4242 + M)
+    mag = 10.0 ** (detrand.uniform((M, K), 77 + M) * 12.0 - 6.0)
+    x = O.f32_to_bf16(O.bf16_to_f32(x) * mag.astype(np.float32))
+    ref = O.qmm_exact(x, w, s, b)
+    y = qvex.quantized_matmul(dev(x), dev(w), dev(s), dev(b))
+    torch.cuda.synchronize()
+    assert rel_l2(host_u16(y), ref) <= MATMUL_TOL
+
+
 def test_qmv_quantized_from_real_weights(qvex):
     # config-2 style weights (N(0, 0.02) quantized), M = 2 verify shape
     w = O.f32_to_bf16(detrand.normal((512, 4096), 21) * 0.02)
