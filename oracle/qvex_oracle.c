@@ -72,6 +72,10 @@ static inline uint16_t f2bf(float f) {
   return (uint16_t)(u >> 16);
 }
 
+/* A NaN scale or bias (a group of NaNs, or an infinite edge) is stored as the quiet NaN
+   0x7FC0: NaN payloads differ between CPU and GPU arithmetic, so the format fixes one. */
+static inline uint16_t f2bf_canon(float f) { return isnan(f) ? (uint16_t)0x7FC0u : f2bf(f); }
+
 void orc_f32_to_bf16(const float* in, uint16_t* out, int64_t n) {
   for (int64_t i = 0; i < n; ++i) out[i] = f2bf(in[i]);
 }
@@ -173,8 +177,8 @@ int orc_quantize(const uint16_t* w, int64_t N, int64_t K, int gs, int variant,
     for (int64_t g = 0; g < G; ++g) {
       float s, b;
       quant_group(w + n * K + g * gs, gs, variant, q, &s, &b);
-      scales[n * G + g] = f2bf(s);
-      biases[n * G + g] = f2bf(b);
+      scales[n * G + g] = f2bf_canon(s);
+      biases[n * G + g] = f2bf_canon(b);
       for (int j = 0; j < gs / 8; ++j) {
         uint32_t v = 0;
         for (int i = 0; i < 8; ++i) v |= (uint32_t)q[j * 8 + i] << (4 * i);

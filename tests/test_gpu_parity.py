@@ -153,6 +153,41 @@ def test_quantize_edge_cases_bit_exact(qvex, variant):
     assert np.array_equal(host_u16(b), b_r)
 
 
+@pytest.mark.parametrize("variant", ["minmax", "zero_exact"])
+def test_quantize_nonfinite_bit_exact(qvex, variant):
+    """NaN and infinite elements: NaN codes clamp to 0, an infinite edge makes the scale
+    infinite; the fast no-clamp path must hand every such group to the exact path."""
+    w = (detrand.normal((6, 256), 5) * 0.02).astype(np.float32)
+    w[0, 5] = np.nan
+    w[0, 70] = np.nan
+    w[0, 71] = np.nan
+    w[1, 3] = np.inf
+    w[2, 64] = -np.inf
+    w[3, :64] = np.nan
+    w[4, 128:192] = np.nan
+    w[4, 130] = 1.0
+    w[5, ::3] = np.nan
+    wb = O.f32_to_bf16(w)
+    wq_r, s_r, b_r = O.quantize(wb, 64, variant)
+    wq, s, b = qvex.quantize(dev(wb), 64, 4, variant=variant)
+    assert np.array_equal(wq.view(torch.int32).cpu().numpy().view(np.uint32), wq_r)
+    assert np.array_equal(host_u16(s), s_r)
+    assert np.array_equal(host_u16(b), b_r)
+
+
+@pytest.mark.parametrize("N,K", [(1000, 4160), (3, 64), (777, 1024), (4099, 576)])
+def test_quantize_ragged_shapes_bit_exact(qvex, N, K):
+    """Group counts that leave a partial last stage (512 groups per stage), one group per
+    row, and more stages than SMs with a ragged tail."""
+    w = O.f32_to_bf16(detrand.normal((N, K), N + K) * 0.05)
+    wq_r, s_r, b_r = O.quantize(w, 64, "minmax")
+    wq, s, b = qvex.quantize(dev(w), 64, 4)
+    torch.cuda.synchronize()
+    assert np.array_equal(wq.view(torch.int32).cpu().numpy().view(np.uint32), wq_r)
+    assert np.array_equal(host_u16(s), s_r)
+    assert np.array_equal(host_u16(b), b_r)
+
+
 def test_pack_order_on_device(qvex, golden_dir):
     # quantize a row whose codes are known, compare the packed words with the reference pack
     z = np.load(golden_dir / "pack_4bit.npz")
