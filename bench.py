@@ -136,7 +136,32 @@ def measure_configs(torch, device, hbm_peak, tc_peak):
     fl = 2.0 * M * N * K
     out["qmm_config2"] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
                           "frac_bf16_dense": round(fl / ms / 1e9 / tc_peak, 3), "M": M, "N": N, "K": K}
+    # batched decode through qmm (M = 64 tokens; the tiles do not fill the SMs, so K is
+    # split across them): five weight copies rotate so that they stream from HBM
+    Mb = 64
+    xb = c["x"][:Mb].contiguous()
+    wqs = [c["wq"]] + [c["wq"].clone() for _ in range(4)]
+    ws_b = torch.empty(qvex.qmm_workspace_size(Mb, N, K), dtype=torch.uint8, device=device)
+    yb = torch.empty((Mb, N), dtype=torch.bfloat16, device=device)
+    it = iter(range(1 << 30))
+    ms = _cuda_time(torch, lambda: qvex.quantized_matmul(xb, wqs[next(it) % 5], c["s"], c["b"], out=yb,
+                                                         workspace=ws_b), 20)
+    wbytes = N * K // 2 + N * (K // 64) * 4
+    out["qmm_batch64"] = {"ms": round(ms, 4), "weight_gbs": round(wbytes / ms / 1e6, 1),
+                          "frac_hbm": round(wbytes / ms / 1e6 / hbm_peak, 3),
+                          "tflops": round(2.0 * Mb * N * K / ms / 1e9, 1), "M": Mb, "N": N, "K": K}
+    del wqs, ws_b, yb, xb
     del c, ws, y
+    # q/k conditioning in front of the recurrence (config-3 shape, T = 2048, B = 8):
+    # bf16 in and out, 4 bytes per element, 268 MB per call
+    g = torch.Generator(device=device)
+    g.manual_seed(4)
+    qk = [torch.randn((8, 2048, 16, 128), device=device, generator=g).to(torch.bfloat16) for _ in range(2)]
+    ms = _cuda_time(torch, lambda: qvex.qk_condition(qk[0], qk[1]), 10)
+    qkb = 2 * qk[0].numel() * 4
+    out["qk_condition_B8_T2048"] = {"ms": round(ms, 4), "gbs": round(qkb / ms / 1e6, 1),
+                                    "frac_hbm": round(qkb / ms / 1e6 / hbm_peak, 3)}
+    del qk
     # gated DeltaNet: decode step (HBM: state in + out) and 2048-step prefill (serial in T)
     for B, T in ((1, 1), (8, 1), (1, 2048), (8, 2048)):
         args = gd_case(torch, device, B, T)

@@ -63,7 +63,10 @@ int qvx_device_status(void* stream, int* device_status);
 int qvx_qmv(const void* x, const uint32_t* w, const void* scales, const void* biases,
             void* y, int M, int N, int K, int group_size, int bits, void* stream);
 
-/* Bytes of workspace qvx_qmm needs for these sizes. */
+/* Bytes of workspace qvx_qmm uses for these sizes.  When the tiles do not fill the SMs
+ * (small M) this includes fp32 partial sums that let qvx_qmm split K across SMs; a
+ * workspace that holds everything but those partial sums is also accepted and runs the
+ * call unsplit (same results within rounding, slower). */
 size_t qvx_qmm_workspace_size(int M, int N, int K);
 
 /* y[M,N] (bf16) = x[M,K] (bf16) @ dequant(w)^T for any M >= 1 (prefill; built for
@@ -82,8 +85,9 @@ int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* bi
  * whose memory pool owns the GPU's memory and forbids cudaMalloc while serving.  The
  * scratch qvx_qmm would take as a workspace is a 16 MiB array built into the library,
  * held by every GPU that loads it until the process exits.  Calls whose
- * qvx_qmm_workspace_size(M, N, K) exceeds 16 MiB fail with QVX_ERR_WORKSPACE; at
- * N = 12288, K = 4096 that is above about M = 1270.  Same results as qvx_qmm.  Every
+ * least workspace (without the K-split partial sums, which it uses only when they
+ * fit) exceeds 16 MiB fail with QVX_ERR_WORKSPACE; at N = 12288, K = 4096 that is above
+ * about M = 1270.  Same results as qvx_qmm.  Every
  * call shares the array, so calls that overlap on the GPU (other streams, other host
  * threads) race: order them.  Nothing in it needs clearing, since each call writes all
  * the scratch it reads.  The first call on each device looks up the array's address;

@@ -26,11 +26,15 @@ __global__ void __launch_bounds__(kQkRows) qk_condition_kernel(const uint16_t* _
   const int wpr = D >> 1;                         // words per row in global memory
   const uint32_t* src = reinterpret_cast<const uint32_t*>(in + r0 * D);
   uint32_t* dst = reinterpret_cast<uint32_t*>(out + r0 * D);
-  const int total_w = nrows * wpr;
 
-  // stage: coalesced 4-byte words (rows are D*2 bytes apart, D even)
+  // stage: coalesced 4-byte words (rows are D*2 bytes apart, D even).  Word i is in row
+  // i / wpr, taken as (i * mdiv) >> 21: exact for i < 2^14 and wpr <= 128 (checked for
+  // every such pair), and cheap enough that the loop's loads stay batched.
+  const int total_w = nrows * wpr;
+  const uint32_t mdiv = (1u << 21) / (uint32_t)wpr + 1u;
+#pragma unroll 4
   for (int i = threadIdx.x; i < total_w; i += kQkRows) {
-    const int r = i / wpr, c = i - r * wpr;
+    const int r = (int)(((uint32_t)i * mdiv) >> 21), c = i - r * wpr;
     qk_smem[r * stride_w + c] = src[i];
   }
   __syncthreads();
@@ -57,8 +61,9 @@ __global__ void __launch_bounds__(kQkRows) qk_condition_kernel(const uint16_t* _
     }
   }
   __syncthreads();
+#pragma unroll 4
   for (int i = threadIdx.x; i < total_w; i += kQkRows) {
-    const int r = i / wpr, c = i - r * wpr;
+    const int r = (int)(((uint32_t)i * mdiv) >> 21), c = i - r * wpr;
     dst[i] = qk_smem[r * stride_w + c];
   }
 }

@@ -17,12 +17,16 @@
 //   [off_fexp]     f     int32 [N]     per weight row exponent
 //   [off_prm]      prm   uint2 [G/2, N padded to 256, 2] fp16 multipliers (S24, S20 | B) of
 //                                        groups (2j, 2j+1), G = K/64 rounded up to even
+//   [off_part]     part  fp32  [P, M, N] partial sums of the K parts, only when the tiles
+//                                        do not fill the SMs (small M, P = qmm_split_parts);
+//                                        a workspace without room for them runs P = 1
 #include "common.cuh"
 
 namespace qvx {
 
 int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, const uint2* prm, const uint32_t* w,
-                  __nv_bfloat16* y, int M, int N, int K, cudaStream_t stream);
+                  __nv_bfloat16* y, int M, int N, int K, int P, float* part, cudaStream_t stream);
+int qmm_split_parts(int M, int N, int K);
 int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm, int N, int K, cudaStream_t stream);
 int qmm_row_pad(int N);
 size_t qmm_prm_bytes(int N, int K);
@@ -34,7 +38,8 @@ int check_qparams(const char* who, const void* x, const uint32_t* w, const void*
 static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct QmmWorkspace {
-  size_t off_x16, off_exp, off_fexp, off_prm, total;
+  size_t off_x16, off_exp, off_fexp, off_prm, off_part, base, total;
+  int parts;
 };
 
 static QmmWorkspace qmm_ws_layout(int M, int N, int K) {
@@ -43,7 +48,10 @@ static QmmWorkspace qmm_ws_layout(int M, int N, int K) {
   l.off_exp = align256((size_t)M * K * sizeof(__half));
   l.off_fexp = l.off_exp + align256((size_t)M * sizeof(int32_t));
   l.off_prm = l.off_fexp + align256((size_t)N * sizeof(int32_t));
-  l.total = l.off_prm + align256(qmm_prm_bytes(N, K));
+  l.off_part = l.off_prm + align256(qmm_prm_bytes(N, K));
+  l.base = l.off_part;
+  l.parts = qmm_split_parts(M, N, K);
+  l.total = l.parts > 1 ? l.off_part + align256((size_t)l.parts * M * N * sizeof(float)) : l.base;
   return l;
 }
 
@@ -107,9 +115,11 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const __nv_bfloat16* __re
 int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
                 int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   const QmmWorkspace l = qmm_ws_layout(M, N, K);
-  if (!workspace || workspace_bytes < l.total)
+  if (!workspace || workspace_bytes < l.base)
     return fail(QVX_ERR_WORKSPACE, "qvx_qmm: workspace of %zu bytes needed, %zu given", l.total,
                 workspace ? workspace_bytes : (size_t)0);
+  // the K parts run only when the caller's workspace holds their partial sums
+  const int parts = workspace_bytes >= l.total ? l.parts : 1;
   if (!aligned(workspace, 256)) return fail(QVX_ERR_ALIGN, "qvx_qmm: workspace must be 256-byte aligned");
   char* ws = static_cast<char*>(workspace);
   __half* x16 = reinterpret_cast<__half*>(ws + l.off_x16);
@@ -121,7 +131,8 @@ int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void
   if (rc) return rc;
   rc = qmm_w_prep(scales, biases, fexp, prm, N, K, stream);
   if (rc) return rc;
-  return qmm_tc_launch(x16, xexp, fexp, prm, w, static_cast<__nv_bfloat16*>(y), M, N, K, stream);
+  float* part = parts > 1 ? reinterpret_cast<float*>(ws + l.off_part) : nullptr;
+  return qmm_tc_launch(x16, xexp, fexp, prm, w, static_cast<__nv_bfloat16*>(y), M, N, K, parts, part, stream);
 }
 
 }  // namespace qvx
@@ -130,6 +141,14 @@ extern "C" size_t qvx_qmm_workspace_size(int M, int N, int K) {
   if (M < 1 || N < 1 || K < 64) return 0;
   return qvx::qmm_ws_layout(M, N, K).total;
 }
+
+namespace qvx {
+// The least workspace qvx_qmm accepts: everything but the K-part partial sums.
+size_t qmm_ws_base_bytes(int M, int N, int K) {
+  if (M < 1 || N < 1 || K < 64) return 0;
+  return qmm_ws_layout(M, N, K).base;
+}
+}  // namespace qvx
 
 extern "C" int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M,
                        int N, int K, int group_size, int bits, void* workspace, size_t workspace_bytes,

@@ -9,14 +9,15 @@
 // can synchronise the device in the middle of a step).
 //
 // The price and the limit: kQmmScratchBytes (16 MiB) of device memory, held by every GPU
-// that loads the library until the process exits.  That fits qvx_qmm_workspace_size(M,
-// N, K) up to about M = 1270 tokens at N = 12288, K = 4096 (14.7 MB at M = 1024); larger
-// calls are rejected with QVX_ERR_WORKSPACE before any GPU work.
+// that loads the library until the process exits.  That fits the least workspace qvx_qmm
+// accepts up to about M = 1270 tokens at N = 12288, K = 4096 (14.7 MB at M = 1024); larger
+// calls are rejected with QVX_ERR_WORKSPACE before any GPU work.  At small M, where
+// qvx_qmm splits K across SMs, the split's partial sums are used only when they fit too.
 //
 // Sharing: every call on a device uses the same array, and it keeps whatever the last
 // call left in it.  Nothing has to start at zero: each call writes every scratch byte it
 // reads (the fp16 copy of x and its row exponents, the weight-row exponents and the group
-// multipliers, padding included) before its main kernel reads them.  Two calls whose
+// multipliers, padding included, and every partial sum of a K split) before it is read.  Two calls whose
 // work overlaps on the GPU -- on different streams, or from different host threads --
 // race on the array and corrupt each other's results; order them (one stream, or events).
 //
@@ -29,6 +30,7 @@ namespace qvx {
 
 int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
                 int K, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+size_t qmm_ws_base_bytes(int M, int N, int K);
 int check_qparams(const char* who, const void* x, const uint32_t* w, const void* s, const void* b, const void* y,
                   int M, int N, int K, int group_size, int bits);
 
@@ -63,7 +65,7 @@ extern "C" int qvx_qmm_noalloc(const void* x, const uint32_t* w, const void* sca
                                int M, int N, int K, int group_size, int bits, void* stream) {
   int rc = qvx::check_qparams("qvx_qmm_noalloc", x, w, scales, biases, y, M, N, K, group_size, bits);
   if (rc) return rc;
-  const size_t need = qvx_qmm_workspace_size(M, N, K);
+  const size_t need = qvx::qmm_ws_base_bytes(M, N, K);
   if (need == 0 || need > qvx::kQmmScratchBytes)
     return qvx::fail(QVX_ERR_WORKSPACE,
                      "qvx_qmm_noalloc: M=%d N=%d K=%d needs %zu bytes of scratch, more than the %zu built into the "

@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_y, const uint2* __restrict__ prm,
                   const int32_t* __restrict__ fexp, const int32_t* __restrict__ xexp, __nv_bfloat16* __restrict__ y,
-                  int M, int N, int K, int n_pad, int* status) {
+                  int M, int N, int K, int n_pad, int P, float* __restrict__ part, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -153,8 +153,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tiles_m = (M + BN - 1) / BN;
   const int tiles_n = (N + BM - 1) / BM;
   const int ntiles = tiles_m * tiles_n;
-  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int total = my_tiles * nks;  // stages this CTA runs
+  // Work item w = tile w / P, K part w % P (stages [p nks / P, (p+1) nks / P)).  P > 1 only
+  // when there are fewer tiles than SMs (small M); the parts then go to fp32 partial sums
+  // `part` [P][M][N], added up by a second kernel.
+  const int nitems = ntiles * P;
+  const int my_tiles = blockIdx.x < nitems ? (nitems - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto ks_begin = [&](int w) { return (w % P) * nks / P; };
+  auto ks_end = [&](int w) { return (w % P + 1) * nks / P; };
+  int total = 0;  // stages this CTA runs
+  for (int lt = 0; lt < my_tiles; ++lt) {
+    const int w = (int)blockIdx.x + lt * (int)gridDim.x;
+    total += ks_end(w) - ks_begin(w);
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NFULL; ++i) mbar_init(&full[i], 1);
@@ -222,7 +232,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool storer = (warp == EPI_WARP0 && lane == 0);  // issues the tile's TMA store
     uint16_t* stage_y = reinterpret_cast<uint16_t*>(smem + OFF_EPI);  // [BN tokens][BM rows] bf16
     for (int lt = 0; lt < my_tiles; ++lt) {
-      const int t = (int)blockIdx.x + lt * (int)gridDim.x;
+      const int w = (int)blockIdx.x + lt * (int)gridDim.x, t = w / P;
+      float* part_p = part ? part + (size_t)(w % P) * M * N : nullptr;
       const int n_base = (t / tiles_m) * BM, m_base = (t % tiles_m) * BN;
       // exponents do not depend on the MMA: fetch them before waiting for the accumulator
       const int n0 = n_base + quarter * 32 + lane, n1 = n0 + 128;
@@ -267,12 +278,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int emax = __reduce_max_sync(0xffffffffu, e_lane[c]);
           const bool fast = fmin + emin >= -126 && fmax + emax <= 127;
           auto put = [&](int j, float val) {
-            const __nv_bfloat16 o = __float2bfloat16_rn(val);
             if (kStaged) {
-              stage_y[(c * 32 + j) * BM + nr] = __bfloat16_as_ushort(o);
+              stage_y[(c * 32 + j) * BM + nr] = __bfloat16_as_ushort(__float2bfloat16_rn(val));
             } else {
               const int m = m_base + c * 32 + j;
-              if (m < M && n < N) y[(size_t)m * N + n] = o;
+              if (m < M && n < N) {
+                if (part_p)
+                  part_p[(size_t)m * N + n] = val;  // a K part: fp32, summed by qmm_split_sum_kernel
+                else
+                  y[(size_t)m * N + n] = __float2bfloat16_rn(val);
+              }
             }
           };
           if (fast) {
@@ -309,9 +324,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       int it = 0;  // stages issued so far
       bool ok = true;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
-        const int t = (int)blockIdx.x + lt * (int)gridDim.x;
+        const int w = (int)blockIdx.x + lt * (int)gridDim.x, t = w / P;
         const int n_base = (t / tiles_m) * BM, m_base = (t % tiles_m) * BN;
-        for (int ks = 0; ks < nks; ++ks, ++it) {
+        for (int ks = ks_begin(w); ks < ks_end(w); ++ks, ++it) {
           const int s = it % S;
           if (!(ok = mbar_wait(&empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, abort_flag, status))) break;
           uint8_t* st = smem + s * STAGE_BYTES;
@@ -340,9 +355,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                mbar_wait(&full_a[i % DQ_GROUPS], (uint32_t)(i / DQ_GROUPS) & 1u, abort_flag, status);
       };
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
+        const int w = (int)blockIdx.x + lt * (int)gridDim.x, ks0 = ks_begin(w), ks1 = ks_end(w);
         if (!(ok = mbar_wait(acc_empty, ((uint32_t)lt & 1u) ^ 1u, abort_flag, status))) break;
         if (!(ok = wait_stage(it))) break;
-        for (int ks = 0; ks < nks; ++ks, ++it) {
+        for (int ks = ks0; ks < ks1; ++ks, ++it) {
           const int s = it % S, a = it % DQ_GROUPS;
           tc_fence_after();
           const uint32_t b_addr = smem_u32(smem + s * STAGE_BYTES);
@@ -352,8 +368,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < BK / 16; ++j)
               tc_mma_ts_f16(tmem + (uint32_t)(h * 128), tmem + A_COL0 + (uint32_t)(a * 2 + h) * 64 + j * 8,
                             smem_desc_sw128(b_addr + (j >> 2) * X_HALF_BYTES + (j & 3) * 32), IDESC,
-                            (ks > 0 || j > 0) ? 1u : 0u);
-          if (ks + 1 < nks) ok = wait_stage(it + 1);
+                            (ks > ks0 || j > 0) ? 1u : 0u);
+          if (ks + 1 < ks1) ok = wait_stage(it + 1);
           tc_commit(&empty[s]);
           if (!ok) break;
         }
@@ -461,8 +477,31 @@ int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm
   return check_launch("qvx_qmm weight prepass");
 }
 
+// y = bf16(sum over the P K parts), in a fixed order (deterministic).
+__global__ void __launch_bounds__(256) qmm_split_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ y,
+                                                            int P, long long mn) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += stride) {
+    float acc = part[i];
+    for (int p = 1; p < P; ++p) acc += part[(size_t)p * mn + i];
+    y[i] = __float2bfloat16_rn(acc);
+  }
+}
+
+// K parts per tile: when the tiles do not fill the SMs (small M), each tile's K range is
+// split so that about one work item runs per SM (at most 16 parts, at least one stage each).
+int qmm_split_parts(int M, int N, int K) {
+  using namespace tc;
+  const int ntiles = ((M + BN - 1) / BN) * ((N + BM - 1) / BM);
+  const int nks = (K + BK - 1) / BK;
+  int P = num_sms() / ntiles;
+  if (P > nks) P = nks;
+  if (P > 16) P = 16;
+  return P < 2 ? 1 : P;
+}
+
 int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, const uint2* prm, const uint32_t* w,
-                  __nv_bfloat16* y, int M, int N, int K, cudaStream_t stream) {
+                  __nv_bfloat16* y, int M, int N, int K, int P, float* part, cudaStream_t stream) {
   using namespace tc;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(QVX_ERR_CUDA, "qvx_qmm: cuTensorMapEncodeTiled unavailable");
@@ -491,7 +530,9 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
   if (r != CUDA_SUCCESS) return fail(QVX_ERR_CUDA, "qvx_qmm: w tensor map encode failed (%d)", (int)r);
   // y [M, N] bf16 written by 256 x 128 TMA stores (clipped at the edges) when its rows are
   // 16-byte multiples; otherwise the epilogue stores elements directly
-  const bool staged = (N % 8 == 0) && aligned(y, 16);
+  if (P > 1 && !part) return fail(QVX_ERR_INVALID, "qvx_qmm: K parts need a partial-sum buffer");
+  if (P < 1) P = 1;
+  const bool staged = P == 1 && (N % 8 == 0) && aligned(y, 16);
   CUtensorMap tmap_y;
   memset(&tmap_y, 0, sizeof(tmap_y));
   if (staged) {
@@ -512,11 +553,17 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
       return fail(QVX_ERR_CUDA, "qvx_qmm: cannot set shared memory size");
     if (dev >= 0 && dev < 64) attr_set[dev][staged] = true;
   }
-  const int ntiles = ((M + BN - 1) / BN) * ((N + BM - 1) / BM);
-  const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  kern<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap_x, tmap_w, tmap_y, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N),
-                                             status);
-  return check_launch("qvx_qmm");
+  const int nitems = ((M + BN - 1) / BN) * ((N + BM - 1) / BM) * P;
+  const int grid = nitems < num_sms() ? nitems : num_sms();
+  kern<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap_x, tmap_w, tmap_y, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N), P,
+                                             P > 1 ? part : nullptr, status);
+  int rc = check_launch("qvx_qmm");
+  if (rc || P == 1) return rc;
+  const long long mn = (long long)M * N;
+  long long blocks = (mn + 255) / 256;
+  if (blocks > (long long)num_sms() * 8) blocks = (long long)num_sms() * 8;
+  qmm_split_sum_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part, y, P, mn);
+  return check_launch("qvx_qmm K-part sum");
 }
 
 }  // namespace qvx

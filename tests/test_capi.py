@@ -62,11 +62,18 @@ def test_qmv_rejects_misaligned_x(L):
 
 
 def test_qmm_workspace_checks(L):
-    need = L.qvx_qmm_workspace_size(64, 128, 256)
-    assert need >= 64 * 256 * 2
-    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, None, 0, None) == 6
-    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, DUMMY, need - 1, None) == 6
-    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, P(4096 + 16), need, None) == 3
+    # K = 64 is one stage, so there is no K split and the size asked for is the minimum
+    need = L.qvx_qmm_workspace_size(64, 128, 64)
+    assert need >= 64 * 64 * 2
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 64, 64, 4, None, 0, None) == 6
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 64, 64, 4, DUMMY, need - 1, None) == 6
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 64, 64, 4, P(4096 + 16), need, None) == 3
+    # K = 256 at one tile splits K, and the size includes the fp32 partial sums; a workspace
+    # without them is accepted (the call runs unsplit), one without the rest is not
+    split = L.qvx_qmm_workspace_size(64, 128, 256)
+    assert split >= L.qvx_qmm_workspace_size(64, 128, 64) + 64 * 128 * 4
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, DUMMY, split - 1, None) != 6
+    assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, DUMMY, 1024, None) == 6
 
 
 def test_gated_delta_rejects_bad_shapes(L):

@@ -331,15 +331,16 @@ def test_gated_delta_in_place_state(qvex):
 
 # ------------------------------------------------------------------ qmm (tensor cores, M > 8)
 
-def qmm_direct(qvex, x, w, s, b):
-    """Call qvx_qmm through the C ABI for any M (including M <= 8)."""
+def qmm_direct(qvex, x, w, s, b, short_by=0):
+    """Call qvx_qmm through the C ABI for any M (including M <= 8), with a workspace
+    `short_by` bytes smaller than qvx_qmm_workspace_size asks for."""
     import ctypes
     from qvex import _lib
     M, K = x.shape
     N = w.shape[0]
     xd, wd, sd, bd = dev(x), dev(w), dev(s), dev(b)
     y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
-    need = _lib.lib().qvx_qmm_workspace_size(M, N, K)
+    need = _lib.lib().qvx_qmm_workspace_size(M, N, K) - short_by
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     P = ctypes.c_void_p
     rc = _lib.lib().qvx_qmm(P(xd.data_ptr()), P(wd.data_ptr()), P(sd.data_ptr()), P(bd.data_ptr()),
@@ -367,6 +368,20 @@ def test_qmm_small_m_direct(qvex, M):
     x, _, w, s, b = qmv_inputs(M, 2048, 384, seed=300 + M)
     ref = O.qmm_exact(x, w, s, b)
     assert rel_l2(qmm_direct(qvex, x, w, s, b), ref) <= MATMUL_TOL
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 1024, 4096), (16, 12288, 4096), (128, 4096, 12288), (33, 520, 2048)])
+def test_qmm_k_split_matches_unsplit(qvex, M, N, K):
+    """Small M: the tiles do not fill the SMs, so qvx_qmm splits K across SMs and sums
+    fp32 partials in the workspace.  A workspace without room for the partials (one byte
+    short) runs the unsplit kernel; both agree with the oracle and with each other."""
+    x, _, w, s, b = qmv_inputs(M, K, N, seed=11 * M + N + K)
+    ref = O.qmm_exact(x, w, s, b)
+    split = qmm_direct(qvex, x, w, s, b)
+    whole = qmm_direct(qvex, x, w, s, b, short_by=1)
+    assert rel_l2(split, ref) <= MATMUL_TOL
+    assert rel_l2(whole, ref) <= MATMUL_TOL
+    assert rel_l2(split, whole) <= MATMUL_TOL
 
 
 def test_qmm_config2_full_size_sampled(qvex):
