@@ -82,6 +82,31 @@ __device__ __forceinline__ void gd_load_step(GdStep& s, const __nv_bfloat16* qp,
   s.b = __bfloat162float(*bp);
 }
 
+// A lane's NPT consecutive state floats as one 16-, 8- or 4-byte access (state pointers are
+// 16-byte aligned, checked on the host, and a lane's slice starts at a multiple of NPT).
+template <int NPT>
+__device__ __forceinline__ void ld_state(const float* p, float (&v)[NPT]) {
+  if constexpr (NPT == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else if constexpr (NPT == 2) {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    v[0] = t.x; v[1] = t.y;
+  } else {
+    v[0] = *p;
+  }
+}
+template <int NPT>
+__device__ __forceinline__ void st_state(float* p, const float (&v)[NPT]) {
+  if constexpr (NPT == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  } else if constexpr (NPT == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  } else {
+    *p = v[0];
+  }
+}
+
 template <int NPT>
 __global__ void __launch_bounds__(kGdWarps * 32) gated_delta_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
@@ -101,9 +126,7 @@ __global__ void __launch_bounds__(kGdWarps * 32) gated_delta_kernel(
   float st[kGdRowsPerWarp][NPT];
 #pragma unroll
   for (int r = 0; r < kGdRowsPerWarp; ++r) {
-    const float* src = state_in + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT;
-#pragma unroll
-    for (int i = 0; i < NPT; ++i) st[r][i] = src[i];
+    ld_state<NPT>(state_in + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT, st[r]);
   }
 
   const size_t qk_step = (size_t)Hk * Dk, v_step = (size_t)Hv * Dv, ab_step = Hv;
@@ -123,9 +146,7 @@ __global__ void __launch_bounds__(kGdWarps * 32) gated_delta_kernel(
     if (state_mid != nullptr && t == T - 1) {
 #pragma unroll
       for (int r = 0; r < kGdRowsPerWarp; ++r) {
-        float* dst = state_mid + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT;
-#pragma unroll
-        for (int i = 0; i < NPT; ++i) dst[i] = st[r][i];
+        st_state<NPT>(state_mid + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT, st[r]);
       }
     }
     const float xa = cur.a + dt;
@@ -166,9 +187,7 @@ __global__ void __launch_bounds__(kGdWarps * 32) gated_delta_kernel(
 
 #pragma unroll
   for (int r = 0; r < kGdRowsPerWarp; ++r) {
-    float* dst = state_out + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT;
-#pragma unroll
-    for (int i = 0; i < NPT; ++i) dst[i] = st[r][i];
+    st_state<NPT>(state_out + ((size_t)n * Dv + dv0 + r) * Dk + lane * NPT, st[r]);
   }
 }
 
