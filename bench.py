@@ -14,7 +14,8 @@ With --gpus N (torchrun, one rank per GPU) each projection is column-sharded: ra
 owns a contiguous 1/N of the output rows (weights, scales, biases), and the shards are
 all-gathered after each projection (strong scaling: total work fixed).  By default the
 all-gather is fused into the qmv kernel (qvx_qmv_allgather: every rank stores its rows
-into every rank's output buffer over NVLink and signals; no NCCL call inside the step);
+into every peer's inbox over NVLink as words tagged with the launch, and copies the
+peers' rows out of its own inbox; no NCCL call inside the step);
 --gather nccl runs the local kernel followed by an NCCL all-gather instead.
 
 Prints ONE JSON line (rank 0).  `--impl reference` times the reference's arithmetic on

@@ -99,34 +99,35 @@ int qvx_qmm_noalloc(const void* x, const uint32_t* w, const void* scales, const 
 
 #define QVX_MAX_RANKS 8
 
-/* Where the outputs of a column-sharded projection go.  Every rank r holds a full output
- * buffer out[r] (bf16 [M, n_total], row stride n_total) and an array of 32-bit signal
- * words indexed by slot; out[] and signal[] are those buffers as mapped in the calling
- * process (peer mappings such as CUDA IPC for r != rank, reachable over NVLink).  epoch
- * points to this rank's own launch counters in device memory, also indexed by slot; the
- * signal words and the epochs start at zero.  slot names the projection: two projections
- * must not share one. */
+/* Where the outputs of a column-sharded projection go.  Rank r owns rows
+ * [r * N, (r + 1) * N) of an n_total = world * N row projection (N even).  out[rank] is
+ * this rank's full output (bf16 [M, n_total], row stride n_total); inbox[r] is rank r's
+ * receive area for this projection (64-bit words [M, n_total / 2], each two bf16 outputs
+ * and a 32-bit launch tag), as mapped in the calling process (peer mappings such as CUDA
+ * IPC for r != rank, reachable over NVLink).  epoch points to this rank's counters in
+ * device memory, two words per slot.  Inboxes and counters start at zero.  slot names the
+ * projection: two projections must not share one.  out[r] for r != rank is not used. */
 typedef struct qvx_gather {
   void* out[QVX_MAX_RANKS];
-  unsigned int* signal[QVX_MAX_RANKS];
+  void* inbox[QVX_MAX_RANKS];
   unsigned int* epoch;
   int world;   /* ranks, 1..QVX_MAX_RANKS */
   int rank;    /* this rank */
-  int n_total; /* rows of the whole projection */
-  int row0;    /* first row of this rank's shard */
-  int slot;    /* signal word and epoch index */
+  int n_total; /* rows of the whole projection (world * N) */
+  int row0;    /* first row of this rank's shard (rank * N) */
+  int slot;    /* index into epoch (two words per slot) */
 } qvx_gather;
 
 /* Column-sharded decode projection with its all-gather fused in: y = x @ dequant(w)^T
- * for this rank's N rows (global rows row0 .. row0+N-1), written into rows [row0, row0+N)
- * of EVERY rank's out buffer by peer stores, then signalled.  When the kernel completes,
- * out[rank] holds all n_total outputs of all ranks.  Replaces the per-projection
- * qvx_qmv + NCCL all-gather of column sharding (the reference runs on one Apple GPU and
- * has no counterpart; the projection it shards is QLinear.__call__, engine/model.py:87-91).
- * Every rank must make the same sequence of calls with the same M, N and K.  M <= 8,
- * K % 512 == 0, scales/biases and every out[r] 16-byte aligned.  A rank that never
- * arrives makes the others give up after 2 s with QVX_ERR_TIMEOUT in the device status
- * word. */
+ * for this rank's N rows, written into out[rank]; each CTA also sends its rows to every
+ * peer's inbox as (two bf16, tag) words and takes the peers' rows for the same row range
+ * out of its own inbox.  When the kernel completes, out[rank] holds all n_total outputs of
+ * all ranks.  Replaces the per-projection qvx_qmv + NCCL all-gather of column sharding
+ * (the reference runs on one Apple GPU and has no counterpart; the projection it shards
+ * is QLinear.__call__, engine/model.py:87-91).  Every rank must make the same sequence of
+ * calls with the same M, N and K.  M <= 8, K % 512 == 0, scales/biases and out[rank]
+ * 16-byte aligned, inboxes 8-byte aligned.  A rank that never arrives makes the others
+ * give up after 2 s with QVX_ERR_TIMEOUT in the device status word. */
 int qvx_qmv_allgather(const void* x, const uint32_t* w, const void* scales, const void* biases,
                       const qvx_gather* g, int M, int N, int K, int group_size, int bits,
                       void* stream);

@@ -81,34 +81,21 @@ __device__ __forceinline__ void reduce_transpose(float* p, int lane) {
 // plain qvx_qmv form.  A copy of qvx_gather in the kernel's parameter space.
 struct QmvGather {
   __nv_bfloat16* out[QVX_MAX_RANKS];
-  unsigned* signal[QVX_MAX_RANKS];
+  unsigned long long* inbox[QVX_MAX_RANKS];
   unsigned* epoch;
   int world, rank, n_total, row0, slot;
 };
 
-// Relaxed: the fence before it orders the data.  (A release form carries its own
-// system-scope fence: measured on B200 at ~3.5 us per signal, on top of the explicit one.)
-__device__ __forceinline__ void red_add_relaxed_sys(unsigned* addr, unsigned v) {
-  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+// Flag-in-data words: a 64-bit store or load is single-copy atomic, so the tag in the high
+// half proves that the two bf16 values in the low half are from the same launch -- no
+// fence and no separate signal.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* addr, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
 }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
   return v;
-}
-
-// dst[0, n) = src[0, n) by one warp; dst and src have the same address mod 16 (every
-// rank's buffer has the same layout and a 256-byte aligned base)
-__device__ __forceinline__ void copy_bf16_segment(__nv_bfloat16* dst, const __nv_bfloat16* src, int n, int lane) {
-  const int head = min(n, (int)(((16u - ((uint32_t)reinterpret_cast<uintptr_t>(src) & 15u)) & 15u) >> 1));
-  if (lane < head) dst[lane] = src[lane];
-  const int nv = (n - head) >> 3;
-  const uint4* s4 = reinterpret_cast<const uint4*>(src + head);
-  uint4* d4 = reinterpret_cast<uint4*>(dst + head);
-  for (int i = lane; i < nv; i += 32) d4[i] = s4[i];
-  const int done = head + nv * 8;
-  if (lane < n - done) dst[done + lane] = src[done + lane];
 }
 
 __device__ __forceinline__ uint32_t dp4a_uu(uint32_t a, uint32_t b, uint32_t c) {
@@ -207,14 +194,15 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
   // so that at any moment the grid streams one contiguous stretch of the weights (measured
   // faster than one contiguous range per CTA).  A gathering launch keeps one contiguous
   // range per CTA, which it copies to the peers in one piece at the end.
-  const int r_begin = gather ? (int)(((long long)blockIdx.x * N) / gridDim.x) : 0;
-  const int r_end = gather ? (int)(((long long)(blockIdx.x + 1) * N) / gridDim.x) : N;
+  // (even boundaries: the gather moves rows in pairs; N is even there)
+  const int r_begin = gather ? (int)(((long long)blockIdx.x * N) / gridDim.x) & ~1 : 0;
+  const int r_end = !gather ? N
+                    : blockIdx.x + 1 == gridDim.x ? N
+                                                 : (int)(((long long)(blockIdx.x + 1) * N) / gridDim.x) & ~1;
   const int nchunks = gather ? (r_end - r_begin + R - 1) / R
                              : ((N + R - 1) / R - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   auto chunk_row = [&](int c) { return gather ? r_begin + c * R : ((int)blockIdx.x + c * (int)gridDim.x) * R; };
 
-  // thread 0 is a compute thread, so it has passed griddepcontrol.wait before it waits here
-  const bool gather_waiter = gather && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -369,43 +357,62 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       if (lane == 0) mbar_arrive(&empty[s]);
     }
     if (gather) {
-      // copy this CTA's row segment of each token to every peer (16-byte stores over
-      // NVLink), then publish it to every rank -- also after an abort, so that the others
-      // do not wait out their timeout for this rank
+      // All-gather by flag-in-data words.  Every rank runs the same grid over its own N
+      // rows, so this CTA's peer twin (same block index) covers the same local rows
+      // [r_begin, r_end) of its shard.  Send this CTA's rows to every peer's inbox as
+      // (two bf16, tag) words, then take the twins' rows out of this rank's inbox once
+      // their tags show this launch.  The tag is the slot's launch count + 1, read after
+      // griddepcontrol.wait; the launch's last CTA advances it.  Also after an abort, so
+      // that the peers do not wait out their timeout for this rank.
+      pdl_wait();
       __syncwarp();
-      const int nrows = r_end - r_begin;
+      const unsigned tag = *reinterpret_cast<volatile unsigned*>(g.epoch + 2 * g.slot) + 1u;
+      const int p0 = r_begin >> 1, p1 = r_end >> 1;  // this CTA's row pairs
+      const size_t nh = (size_t)(g.n_total >> 1);     // pairs per token row
       for (int m = 0; m < mc; ++m) {
-        const size_t at = (size_t)(m0 + m) * g.n_total + g.row0 + r_begin;
-        for (int q = 0; q < g.world; ++q)
-          if (q != g.rank) copy_bf16_segment(g.out[q] + at, g.out[g.rank] + at, nrows, lane);
+        const uint32_t* own = reinterpret_cast<const uint32_t*>(g.out[g.rank] + (size_t)(m0 + m) * g.n_total);
+        for (int j = p0 + lane; j < p1; j += 32) {
+          const size_t pair = (size_t)(g.row0 >> 1) + j;
+          const unsigned long long word = (unsigned long long)own[pair] | ((unsigned long long)tag << 32);
+          for (int q = 0; q < g.world; ++q)
+            if (q != g.rank) st_relaxed_sys_u64(g.inbox[q] + (size_t)(m0 + m) * nh + pair, word);
+        }
       }
-      // every lane's peer stores are ordered before the signals by its own fence
-      fence_acq_rel_sys();
+      const unsigned long long t0 = globaltimer_ns();
+      bool late = false;
+      for (int q = 0; q < g.world && !late; ++q) {
+        if (q == g.rank) continue;
+        for (int m = 0; m < mc && !late; ++m) {
+          uint32_t* dst = reinterpret_cast<uint32_t*>(g.out[g.rank] + (size_t)(m0 + m) * g.n_total);
+          for (int j = p0 + lane; j < p1 && !late; j += 32) {
+            const size_t pair = (size_t)(q * N >> 1) + j;  // shards are equal: peer q starts at q N
+            const unsigned long long* src = g.inbox[g.rank] + (size_t)(m0 + m) * nh + pair;
+            unsigned long long word = ld_relaxed_sys_u64(src);
+            for (uint32_t it = 1; (unsigned)(word >> 32) != tag; ++it) {
+              if ((it & 63) == 0 && (globaltimer_ns() - t0 > kWaitTimeoutNs || it > kWaitMaxPolls)) {
+                set_device_status(status, QVX_ERR_TIMEOUT);
+                late = true;
+                break;
+              }
+              word = ld_relaxed_sys_u64(src);
+            }
+            if (!late) dst[pair] = (uint32_t)word;
+          }
+        }
+      }
       __syncwarp();
-      if (lane == 0)
-        for (int q = 0; q < g.world; ++q) red_add_relaxed_sys(g.signal[q] + g.slot, 1u);
+      if (lane == 0) {
+        // count this CTA; the last one of the launch advances the slot's tag (every CTA has
+        // read it by then: a CTA reads it before it counts itself)
+        const unsigned prev = atomicAdd(g.epoch + 2 * g.slot + 1, 1u);
+        if (prev + 1u == gridDim.x * gridDim.y) {
+          g.epoch[2 * g.slot + 1] = 0u;
+          g.epoch[2 * g.slot] = tag;
+        }
+      }
     }
   }
   __syncthreads();
-  if (gather_waiter) {
-    // the grid completes only once every CTA of every rank has published this launch, so
-    // completion of the kernel means out[rank] holds all n_total rows.  The slot's launch
-    // count is read after griddepcontrol.wait: an earlier launch of the same slot may be the
-    // kernel this one overlapped with.
-    const unsigned epoch0 = *reinterpret_cast<volatile unsigned*>(g.epoch + g.slot);
-    const unsigned target = (epoch0 + 1u) * (unsigned)g.world * gridDim.x * gridDim.y;
-    const unsigned* sig = g.signal[g.rank] + g.slot;
-    const unsigned long long t0 = globaltimer_ns();
-    for (uint32_t it = 0;; ++it) {
-      if ((int)(ld_acquire_sys(sig) - target) >= 0) break;
-      if ((it & 63) == 0 && (globaltimer_ns() - t0 > kWaitTimeoutNs || it > kWaitMaxPolls)) {
-        set_device_status(status, QVX_ERR_TIMEOUT);
-        break;
-      }
-    }
-    g.epoch[g.slot] = epoch0 + 1u;
-    __threadfence();
-  }
 }
 
 template <int MC, int RT, bool FULLK, int S>
@@ -508,9 +515,17 @@ extern "C" int qvx_qmv_allgather(const void* x, const uint32_t* w, const void* s
   if (g->slot < 0 || g->row0 < 0 || (long long)g->row0 + N > (long long)g->n_total)
     return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: rows [%d, %d) outside the %d-row projection (slot %d)",
                 g->row0, g->row0 + N, g->n_total, g->slot);
+  // equal shards in rank order, rows moved in pairs
+  if (N % 2 != 0 || (long long)g->n_total != (long long)g->world * N || g->row0 != g->rank * N)
+    return fail(QVX_ERR_INVALID,
+                "qvx_qmv_allgather: needs equal shards of an even row count in rank order (N=%d, n_total=%d, "
+                "world=%d, rank=%d, row0=%d)",
+                N, g->n_total, g->world, g->rank, g->row0);
+  if (!g->out[g->rank] || !aligned(g->out[g->rank], 16))
+    return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: missing or misaligned output of this rank");
   for (int q = 0; q < g->world; ++q)
-    if (!g->out[q] || !g->signal[q] || !aligned(g->out[q], 16) || !aligned(g->signal[q], 4))
-      return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: missing or misaligned buffer of rank %d", q);
+    if (!g->inbox[q] || !aligned(g->inbox[q], 8))
+      return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: missing or misaligned inbox of rank %d", q);
   if (!g->epoch || !aligned(g->epoch, 4)) return fail(QVX_ERR_INVALID, "qvx_qmv_allgather: missing epoch counters");
   int rc = check_qparams("qvx_qmv_allgather", x, w, scales, biases, g->out[g->rank], M, N, K, group_size, bits);
   if (rc) return rc;
@@ -518,7 +533,7 @@ extern "C" int qvx_qmv_allgather(const void* x, const uint32_t* w, const void* s
   QmvGather d;
   for (int q = 0; q < QVX_MAX_RANKS; ++q) {
     d.out[q] = q < g->world ? static_cast<__nv_bfloat16*>(g->out[q]) : nullptr;
-    d.signal[q] = q < g->world ? g->signal[q] : nullptr;
+    d.inbox[q] = q < g->world ? static_cast<unsigned long long*>(g->inbox[q]) : nullptr;
   }
   d.epoch = g->epoch;
   d.world = g->world;

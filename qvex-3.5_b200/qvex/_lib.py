@@ -47,9 +47,10 @@ QVX_MAX_RANKS = 8
 
 
 class QvxGather(ctypes.Structure):
-    """Mirror of ``qvx_gather`` (include/qvex.h): peer output buffers and signal words of
-    a column-sharded projection, this rank's epoch counters, and its place in the rows."""
-    _fields_ = [("out", _P * QVX_MAX_RANKS), ("signal", _P * QVX_MAX_RANKS), ("epoch", _P),
+    """Mirror of ``qvx_gather`` (include/qvex.h): the output buffers and receive areas
+    (inboxes) of a column-sharded projection, this rank's launch counters, and its place in
+    the rows."""
+    _fields_ = [("out", _P * QVX_MAX_RANKS), ("inbox", _P * QVX_MAX_RANKS), ("epoch", _P),
                 ("world", _I), ("rank", _I), ("n_total", _I), ("row0", _I), ("slot", _I)]
 
 

@@ -8,10 +8,11 @@ nonlinearity that pairs components -- SwiGLU over gate|up, the DeltaNet split of
 qkv|z|b|a -- finds both halves of its inputs on the same rank.
 
 For decode (M <= 8) the all-gather can instead be fused into the projection kernel
-(``qvx_qmv_allgather``): every rank stores its rows straight into every rank's output
-buffer over NVLink and signals a per-projection counter, so one kernel per projection
-does the compute and the exchange, with no NCCL call.  ``PeerGather`` sets up those
-buffers: one device allocation per rank, mapped into every rank's process with CUDA IPC.
+(``qvx_qmv_allgather``): every rank stores its rows straight into every peer's receive
+area (inbox) over NVLink as words that carry their launch's tag, and takes the peers'
+rows out of its own inbox, so one kernel per projection does the compute and the
+exchange, with no fence, signal or NCCL call.  ``PeerGather`` sets up those buffers: one
+device allocation per rank, mapped into every rank's process with CUDA IPC.
 
 The pieces are separate so the host logic runs on CPU process groups (gloo) in tests:
 ``shard_rows`` / ``shard_linear`` / ``shard_fused`` only slice, ``gather_columns`` only
@@ -78,9 +79,10 @@ GATHER_ALIGN = 256
 GATHER_M_MAX = 8  # tokens a fused decode projection gathers (qvx_qmv's M <= 8)
 
 
-def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], int]:
-    """Byte layout of one rank's PeerGather buffer: a 32-bit signal word per region (slot),
-    padded to 256 bytes, then the regions, each 256-byte aligned.  Returns the regions'
+def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], list[int], int]:
+    """Byte layout of one rank's PeerGather buffer: per slot, the full output (``region_bytes``
+    of bf16) and then its inbox (twice that: one 64-bit word, two outputs and a tag, per
+    output pair), each 256-byte aligned.  Returns the outputs' offsets, the inboxes'
     offsets and the total size."""
     if any(b <= 0 for b in region_bytes):
         raise ValueError("every region needs a positive size")
@@ -88,24 +90,26 @@ def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], int]:
     def up(v):
         return (v + GATHER_ALIGN - 1) // GATHER_ALIGN * GATHER_ALIGN
 
-    at = up(4 * len(region_bytes))
-    offsets = []
+    at = 0
+    outs, inboxes = [], []
     for b in region_bytes:
-        offsets.append(at)
+        outs.append(at)
         at = up(at + b)
-    return offsets, at
+        inboxes.append(at)
+        at = up(at + 2 * b)
+    return outs, inboxes, at
 
 
-def gather_descriptor(bases: list[int], offset: int, epoch_ptr: int, rank: int, slot: int, n_total: int,
-                      row0: int):
-    """qvx_gather for one projection: out[r] = rank r's buffer + the slot's region offset;
-    signal[r] = rank r's buffer itself (the signal words lead it and the kernel indexes
-    them by slot); epoch = this rank's counters (also indexed by slot in the kernel)."""
+def gather_descriptor(bases: list[int], out_offset: int, inbox_offset: int, epoch_ptr: int, rank: int,
+                      slot: int, n_total: int, row0: int):
+    """qvx_gather for one projection: out[r] and inbox[r] = rank r's buffer + the slot's
+    output and inbox offsets; epoch = this rank's counters (two words per slot, indexed by
+    slot in the kernel)."""
     from . import _lib
     d = _lib.QvxGather()
     for r, base in enumerate(bases):
-        d.out[r] = base + offset
-        d.signal[r] = base
+        d.out[r] = base + out_offset
+        d.inbox[r] = base + inbox_offset
     d.epoch = epoch_ptr
     d.world, d.rank, d.n_total, d.row0, d.slot = len(bases), rank, n_total, row0, slot
     return d
@@ -128,7 +132,7 @@ class _DeviceArray:
 
 
 class PeerGather:
-    """Output regions and signal words of fused column-sharded projections, one device
+    """Output regions and inboxes of fused column-sharded projections, one device
     buffer per rank of ``group`` mapped into every rank's process (CUDA IPC; peer access
     over NVLink).  ``region_bytes[i]`` is the size of slot i's full output; every rank must
     construct it with the same list, and keep it alive while its projections are in use.
@@ -145,7 +149,7 @@ class PeerGather:
             raise ValueError(f"{self.world} ranks; the fused gather supports up to {_lib.QVX_MAX_RANKS}")
         self.device = torch.cuda.current_device()
         _ck(rt.cudaSetDevice(self.device))
-        self.offsets, self.nbytes = plan_gather_layout(region_bytes)
+        self.offsets, self.inboxes, self.nbytes = plan_gather_layout(region_bytes)
         self.slots = len(region_bytes)
         self._own = _ck(rt.cudaMalloc(self.nbytes))
         _ck(rt.cudaMemset(self._own, 0, self.nbytes))
@@ -161,7 +165,7 @@ class PeerGather:
                 h = rt.cudaIpcMemHandle_t()
                 h.reserved = hb
                 self.base.append(int(_ck(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))))
-        self.epoch = torch.zeros(max(1, self.slots), dtype=torch.int32, device=self.device)
+        self.epoch = torch.zeros(2 * max(1, self.slots), dtype=torch.int32, device=self.device)
         self._next = 0
         dist.barrier(group)  # every rank has mapped every buffer before anyone stores
 
@@ -173,8 +177,8 @@ class PeerGather:
         return self._next - 1
 
     def descriptor(self, slot: int, n_total: int, row0: int):
-        return gather_descriptor(self.base, self.offsets[slot], self.epoch.data_ptr(), self.rank, slot, n_total,
-                                 row0)
+        return gather_descriptor(self.base, self.offsets[slot], self.inboxes[slot], self.epoch.data_ptr(),
+                                 self.rank, slot, n_total, row0)
 
     def output(self, slot: int, M: int, n_total: int) -> torch.Tensor:
         """This rank's full output of ``slot`` as a bf16 [M, n_total] tensor (a view of the
@@ -200,7 +204,7 @@ class PeerGather:
 
 def qmv_allgather(local: QLinear, x: torch.Tensor, desc) -> None:
     """One fused launch: this rank's rows of ``local`` times x [M <= 8, K], stored into every
-    rank's output region of ``desc`` (a PeerGather descriptor) and signalled."""
+    rank's output region of ``desc`` (a PeerGather descriptor) through the inboxes."""
     from . import _lib
     if x.dtype != torch.bfloat16 or not x.is_cuda:
         raise ValueError("x must be a bf16 CUDA tensor")

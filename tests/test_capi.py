@@ -128,7 +128,7 @@ def test_qmv_allgather_rejects_bad_descriptors(L):
     g = _lib.QvxGather()
     for r in range(2):
         g.out[r] = 4096
-        g.signal[r] = 4096
+        g.inbox[r] = 4096
     g.epoch = 4096
     g.world, g.rank, g.n_total, g.row0, g.slot = 2, 0, 16, 0, 0
 
@@ -143,10 +143,18 @@ def test_qmv_allgather_rejects_bad_descriptors(L):
     g.rank = 1
     g.row0 = 12
     assert call(g) == 1            # rows past n_total
+    g.row0 = 4
+    assert call(g) == 1            # shards not in rank order
     g.row0 = 8
-    g.signal[1] = None
-    assert call(g) == 1            # a peer buffer missing
-    g.signal[1] = 4096
+    assert call(g, N=6) == 1       # shards not equal (2 x 6 != 16)
+    g.n_total = 14
+    assert call(g, N=7) == 1       # odd row count: rows move in pairs
+    g.n_total = 16
+    g.inbox[0] = None
+    assert call(g) == 1            # a peer's inbox missing
+    g.inbox[0] = 4100
+    assert call(g) == 1            # an inbox not 8-byte aligned
+    g.inbox[0] = 4096
     assert call(g, M=9) == 1       # decode only
     assert ctypes.sizeof(_lib.QvxGather) == 160  # 8 + 8 pointers, epoch, 5 ints (+4 padding)
 

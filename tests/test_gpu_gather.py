@@ -5,7 +5,9 @@ a gloo process group: no NCCL) and run sharded projections; each rank's gathered
 must equal, bit for bit, the single-GPU qvx_qmv of the unsharded weights (a row's
 arithmetic does not depend on how rows are split).  Covered: M = 1, 3 and 8, two calls in
 a row with different inputs, the same projection launched twice back to back (the
-second launch overlaps the first through programmatic dependent launch), and slot
+second launch overlaps the first through programmatic dependent launch), one projection
+called with a different token count in between (another grid, so another set of CTAs
+writes each inbox word: the launch tags must still tell old words from new), and slot
 numbers above 120.  Skipped with fewer than two GPUs.
 """
 import os
@@ -36,8 +38,8 @@ def _child(rank, world, port, q):
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60))
         qvex.load_library()
-        # 120 unused slots first: the projections below use slots past the signal words'
-        # 256-byte padding, where a descriptor addressing mistake would land in an output region
+        # 120 unused slots first: the projections below use high slot numbers, so a mistake in
+        # the per-slot counters or region offsets lands in someone else's memory
         peer = PeerGather([256] * 120 + [8 * N * 2 for _, _, N in CASES])
         for _ in range(120):
             peer.reserve()
@@ -46,12 +48,13 @@ def _child(rank, world, port, q):
         for M, K, N in CASES:
             x1, _, w, s, b = qmv_inputs(M, K, N, seed=500 + N)
             x2 = qmv_inputs(M, K, N, seed=900 + N)[0]
+            x3 = qmv_inputs(4 if M == 1 else 1, K, N, seed=700 + N)[0]  # another token count
 
             def dev(a):
                 return torch.from_numpy(np.ascontiguousarray(a)).cuda()
             full = QLinear(dev(w).view(torch.int32), dev(s).view(torch.bfloat16), dev(b).view(torch.bfloat16))
             lin = ShardedQLinear(full, rank=rank, world=world, peer=peer)
-            for xa in (x1, x2, x2):
+            for xa in (x1, x2, x2, x3, x1):
                 xt = dev(xa).view(torch.bfloat16)
                 y = lin(xt).clone()
                 ref = full(xt)

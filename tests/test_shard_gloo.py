@@ -128,25 +128,30 @@ def test_shard_rows_rules():
 
 def test_plan_gather_layout():
     from qvex.shard import plan_gather_layout
-    offs, total = plan_gather_layout([2 * 1024, 300, 16])
-    assert offs[0] == 256                      # 3 signal words, padded
-    assert all(o % 256 == 0 for o in offs)
-    assert offs[1] == offs[0] + 2048 and offs[2] == offs[1] + 512
-    assert total == offs[2] + 256
+    outs, inboxes, total = plan_gather_layout([2 * 1024, 300, 16])
+    assert outs[0] == 0
+    assert all(o % 256 == 0 for o in outs + inboxes)
+    # each slot: its output, then an inbox twice its size
+    assert inboxes[0] == 2048 and outs[1] == inboxes[0] + 4096
+    assert inboxes[1] == outs[1] + 512 and outs[2] == inboxes[1] + 768
+    assert inboxes[2] == outs[2] + 256 and total == inboxes[2] + 256
     with pytest.raises(ValueError):
         plan_gather_layout([0])
 
 
 def test_gather_descriptor_addresses():
-    """Signal words lead each rank's buffer and are indexed by slot in the kernel, so the
-    descriptor carries the buffer base, never base + slot (which would shift slot s to
-    word 2s and, past the padding, into the first output region)."""
+    """Every rank's output and inbox of a slot sit at the same offsets of that rank's buffer;
+    the descriptor carries them per rank, and the counters of this rank."""
     from qvex.shard import gather_descriptor, plan_gather_layout
-    offs, _ = plan_gather_layout([2 * 4096] * 150)
+    outs, inboxes, total = plan_gather_layout([2 * 4096] * 150)
     bases = [1 << 40, 2 << 40]
     for slot in (0, 97, 149):
-        d = gather_descriptor(bases, offs[slot], 12345 << 8, 1, slot, 8192, 4096)
-        assert [d.signal[r] for r in range(2)] == bases
-        assert [d.out[r] for r in range(2)] == [b + offs[slot] for b in bases]
+        d = gather_descriptor(bases, outs[slot], inboxes[slot], 12345 << 8, 1, slot, 8192, 4096)
+        assert [d.out[r] for r in range(2)] == [b + outs[slot] for b in bases]
+        assert [d.inbox[r] for r in range(2)] == [b + inboxes[slot] for b in bases]
         assert d.epoch == 12345 << 8 and d.slot == slot and d.world == 2 and d.rank == 1
-        assert 4 * slot < offs[0]  # the kernel's signal word for this slot precedes every region
+        # a slot's inbox lies between its output and the next slot's output
+        nxt = outs[slot + 1] if slot + 1 < 150 else total
+        assert outs[slot] + 2 * 4096 <= inboxes[slot] and inboxes[slot] + 4 * 4096 <= nxt
+
+
