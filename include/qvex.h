@@ -63,10 +63,11 @@ int qvx_device_status(void* stream, int* device_status);
 int qvx_qmv(const void* x, const uint32_t* w, const void* scales, const void* biases,
             void* y, int M, int N, int K, int group_size, int bits, void* stream);
 
-/* Bytes of workspace qvx_qmm uses for these sizes.  When the tiles do not fill the SMs
- * (small M) this includes fp32 partial sums that let qvx_qmm split K across SMs; a
- * workspace that holds everything but those partial sums is also accepted and runs the
- * call unsplit (same results within rounding, slower). */
+/* Bytes of workspace qvx_qmm uses for these sizes.  When the tiles leave SMs idle (small
+ * M, or a last round of tiles that fills only part of the SMs) this includes fp32
+ * partial sums that let qvx_qmm split those tiles along K across SMs; a workspace that
+ * holds everything but the partial sums is also accepted and runs the call unsplit
+ * (same results within rounding, slower). */
 size_t qvx_qmm_workspace_size(int M, int N, int K);
 
 /* y[M,N] (bf16) = x[M,K] (bf16) @ dequant(w)^T for any M >= 1 (prefill; built for

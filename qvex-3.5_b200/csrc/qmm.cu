@@ -17,16 +17,16 @@
 //   [off_fexp]     f     int32 [N]     per weight row exponent
 //   [off_prm]      prm   uint2 [G/2, N padded to 256, 2] fp16 multipliers (S24, S20 | B) of
 //                                        groups (2j, 2j+1), G = K/64 rounded up to even
-//   [off_part]     part  fp32  [P, M, N] partial sums of the K parts, only when the tiles
-//                                        do not fill the SMs (small M, P = qmm_split_parts);
-//                                        a workspace without room for them runs P = 1
+//   [off_part]     part  fp32  [tail tiles, P, 128 tokens, 256 rows] partial sums of the K
+//                                        parts of the tiles in a last, partly filled round
+//                                        (all tiles at small M; qmm_split_plan); a
+//                                        workspace without room for them runs unsplit
 #include "common.cuh"
 
 namespace qvx {
 
 int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, const uint2* prm, const uint32_t* w,
-                  __nv_bfloat16* y, int M, int N, int K, int P, float* part, cudaStream_t stream);
-int qmm_split_parts(int M, int N, int K);
+                  __nv_bfloat16* y, int M, int N, int K, const QmmSplit& sp, float* part, cudaStream_t stream);
 int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm, int N, int K, cudaStream_t stream);
 int qmm_row_pad(int N);
 size_t qmm_prm_bytes(int N, int K);
@@ -39,7 +39,7 @@ static inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct QmmWorkspace {
   size_t off_x16, off_exp, off_fexp, off_prm, off_part, base, total;
-  int parts;
+  QmmSplit split;
 };
 
 static QmmWorkspace qmm_ws_layout(int M, int N, int K) {
@@ -50,8 +50,8 @@ static QmmWorkspace qmm_ws_layout(int M, int N, int K) {
   l.off_prm = l.off_fexp + align256((size_t)N * sizeof(int32_t));
   l.off_part = l.off_prm + align256(qmm_prm_bytes(N, K));
   l.base = l.off_part;
-  l.parts = qmm_split_parts(M, N, K);
-  l.total = l.parts > 1 ? l.off_part + align256((size_t)l.parts * M * N * sizeof(float)) : l.base;
+  l.split = qmm_split_plan(M, N, K);
+  l.total = l.split.P > 1 ? l.off_part + align256(l.split.part_bytes) : l.base;
   return l;
 }
 
@@ -119,7 +119,11 @@ int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void
     return fail(QVX_ERR_WORKSPACE, "qvx_qmm: workspace of %zu bytes needed, %zu given", l.total,
                 workspace ? workspace_bytes : (size_t)0);
   // the K parts run only when the caller's workspace holds their partial sums
-  const int parts = workspace_bytes >= l.total ? l.parts : 1;
+  QmmSplit split = l.split;
+  if (workspace_bytes < l.total) {
+    split.P = 1;
+    split.F = split.ntiles;
+  }
   if (!aligned(workspace, 256)) return fail(QVX_ERR_ALIGN, "qvx_qmm: workspace must be 256-byte aligned");
   char* ws = static_cast<char*>(workspace);
   __half* x16 = reinterpret_cast<__half*>(ws + l.off_x16);
@@ -131,8 +135,8 @@ int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void
   if (rc) return rc;
   rc = qmm_w_prep(scales, biases, fexp, prm, N, K, stream);
   if (rc) return rc;
-  float* part = parts > 1 ? reinterpret_cast<float*>(ws + l.off_part) : nullptr;
-  return qmm_tc_launch(x16, xexp, fexp, prm, w, static_cast<__nv_bfloat16*>(y), M, N, K, parts, part, stream);
+  float* part = split.P > 1 ? reinterpret_cast<float*>(ws + l.off_part) : nullptr;
+  return qmm_tc_launch(x16, xexp, fexp, prm, w, static_cast<__nv_bfloat16*>(y), M, N, K, split, part, stream);
 }
 
 }  // namespace qvx

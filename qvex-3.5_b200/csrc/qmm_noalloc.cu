@@ -11,8 +11,9 @@
 // The price and the limit: kQmmScratchBytes (16 MiB) of device memory, held by every GPU
 // that loads the library until the process exits.  That fits the least workspace qvx_qmm
 // accepts up to about M = 1270 tokens at N = 12288, K = 4096 (14.7 MB at M = 1024); larger
-// calls are rejected with QVX_ERR_WORKSPACE before any GPU work.  At small M, where
-// qvx_qmm splits K across SMs, the split's partial sums are used only when they fit too.
+// calls are rejected with QVX_ERR_WORKSPACE before any GPU work.  Where qvx_qmm splits
+// tiles along K (small M, and the tiles of a last, partly filled round), the split's
+// partial sums are used only when they fit too.
 //
 // Sharing: every call on a device uses the same array, and it keeps whatever the last
 // call left in it.  Nothing has to start at zero: each call writes every scratch byte it

@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_y, const uint2* __restrict__ prm,
                   const int32_t* __restrict__ fexp, const int32_t* __restrict__ xexp, __nv_bfloat16* __restrict__ y,
-                  int M, int N, int K, int n_pad, int P, float* __restrict__ part, int* status) {
+                  int M, int N, int K, int n_pad, int F, int P, float* __restrict__ part, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -153,13 +153,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tiles_m = (M + BN - 1) / BN;
   const int tiles_n = (N + BM - 1) / BM;
   const int ntiles = tiles_m * tiles_n;
-  // Work item w = tile w / P, K part w % P (stages [p nks / P, (p+1) nks / P)).  P > 1 only
-  // when there are fewer tiles than SMs (small M); the parts then go to fp32 partial sums
-  // `part` [P][M][N], added up by a second kernel.
-  const int nitems = ntiles * P;
+  // Work items: items 0 .. F-1 are whole tiles (F is a multiple of the grid: full rounds);
+  // the remaining ntiles - F tiles, which would leave most SMs idle in a last round, are
+  // each split into P parts along K: item F + P tt + p is part p (stages
+  // [p nks / P, (p+1) nks / P)) of tile F + tt.  A part writes fp32 partial sums to its
+  // own tile-shaped buffer part + (item - F) * BM * BN ([BN tokens][BM rows]), added up by
+  // qmm_tail_sum_kernel.  Small M (fewer tiles than SMs) is F = 0.
+  const int nitems = F + (ntiles - F) * P;
   const int my_tiles = blockIdx.x < nitems ? (nitems - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  auto ks_begin = [&](int w) { return (w % P) * nks / P; };
-  auto ks_end = [&](int w) { return (w % P + 1) * nks / P; };
+  auto item_tile = [&](int w) { return w < F ? w : F + (w - F) / P; };
+  auto ks_begin = [&](int w) { return w < F ? 0 : ((w - F) % P) * nks / P; };
+  auto ks_end = [&](int w) { return w < F ? nks : ((w - F) % P + 1) * nks / P; };
   int total = 0;  // stages this CTA runs
   for (int lt = 0; lt < my_tiles; ++lt) {
     const int w = (int)blockIdx.x + lt * (int)gridDim.x;
@@ -232,8 +236,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool storer = (warp == EPI_WARP0 && lane == 0);  // issues the tile's TMA store
     uint16_t* stage_y = reinterpret_cast<uint16_t*>(smem + OFF_EPI);  // [BN tokens][BM rows] bf16
     for (int lt = 0; lt < my_tiles; ++lt) {
-      const int w = (int)blockIdx.x + lt * (int)gridDim.x, t = w / P;
-      float* part_p = part ? part + (size_t)(w % P) * M * N : nullptr;
+      const int w = (int)blockIdx.x + lt * (int)gridDim.x, t = item_tile(w);
+      float* part_p = w >= F ? part + (size_t)(w - F) * (BM * BN) : nullptr;
       const int n_base = (t / tiles_m) * BM, m_base = (t % tiles_m) * BN;
       // exponents do not depend on the MMA: fetch them before waiting for the accumulator
       const int n0 = n_base + quarter * 32 + lane, n1 = n0 + 128;
@@ -278,16 +282,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int emax = __reduce_max_sync(0xffffffffu, e_lane[c]);
           const bool fast = fmin + emin >= -126 && fmax + emax <= 127;
           auto put = [&](int j, float val) {
-            if (kStaged) {
+            if (part_p) {
+              part_p[(c * 32 + j) * BM + nr] = val;  // a K part: fp32, summed by qmm_tail_sum_kernel
+            } else if (kStaged) {
               stage_y[(c * 32 + j) * BM + nr] = __bfloat16_as_ushort(__float2bfloat16_rn(val));
             } else {
               const int m = m_base + c * 32 + j;
-              if (m < M && n < N) {
-                if (part_p)
-                  part_p[(size_t)m * N + n] = val;  // a K part: fp32, summed by qmm_split_sum_kernel
-                else
-                  y[(size_t)m * N + n] = __float2bfloat16_rn(val);
-              }
+              if (m < M && n < N) y[(size_t)m * N + n] = __float2bfloat16_rn(val);
             }
           };
           if (fast) {
@@ -312,8 +313,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) mbar_arrive(epi_full);
         if (storer) {
           if (!mbar_wait(epi_full, (uint32_t)lt & 1u, abort_flag, status)) break;
-          tma_tile_2d_s2g(&tmap_y, smem_u32(stage_y), n_base, m_base);
-          bulk_commit_group();
+          if (!part_p) {  // a K part wrote its partial sums directly
+            tma_tile_2d_s2g(&tmap_y, smem_u32(stage_y), n_base, m_base);
+            bulk_commit_group();
+          }
         }
       }
     }
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int it = 0;  // stages issued so far
       bool ok = true;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
-        const int w = (int)blockIdx.x + lt * (int)gridDim.x, t = w / P;
+        const int w = (int)blockIdx.x + lt * (int)gridDim.x, t = item_tile(w);
         const int n_base = (t / tiles_m) * BM, m_base = (t % tiles_m) * BN;
         for (int ks = ks_begin(w); ks < ks_end(w); ++ks, ++it) {
           const int s = it % S;
@@ -477,31 +480,53 @@ int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm
   return check_launch("qvx_qmm weight prepass");
 }
 
-// y = bf16(sum over the P K parts), in a fixed order (deterministic).
-__global__ void __launch_bounds__(256) qmm_split_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ y,
-                                                            int P, long long mn) {
+// y of the split tail tiles = bf16(sum of their P parts), in a fixed order (deterministic).
+// Element e of the parts' tile space: tile tt = e / (BM BN), token e / BM % BN, row e % BM.
+__global__ void __launch_bounds__(256) qmm_tail_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ y,
+                                                           int M, int N, int F, int P, int ntail) {
+  using namespace tc;
+  const int tiles_m = (M + BN - 1) / BN;
+  const long long total = (long long)ntail * BM * BN;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += stride) {
-    float acc = part[i];
-    for (int p = 1; p < P; ++p) acc += part[(size_t)p * mn + i];
-    y[i] = __float2bfloat16_rn(acc);
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+    const int tt = (int)(e / (BM * BN)), within = (int)(e % (BM * BN));
+    const int t = F + tt, tok = within / BM, row = within % BM;
+    const int m = (t % tiles_m) * BN + tok, n = (t / tiles_m) * BM + row;
+    if (m >= M || n >= N) continue;
+    const float* src = part + (size_t)tt * P * (BM * BN) + within;
+    float acc = src[0];
+    for (int p = 1; p < P; ++p) acc += src[(size_t)p * (BM * BN)];
+    y[(size_t)m * N + n] = __float2bfloat16_rn(acc);
   }
 }
 
-// K parts per tile: when the tiles do not fill the SMs (small M), each tile's K range is
-// split so that about one work item runs per SM (at most 16 parts, at least one stage each).
-int qmm_split_parts(int M, int N, int K) {
+// How the tiles are laid out over the SMs: whole tiles for the full rounds (F of them, a
+// multiple of the SM count), and the tiles of a last, partly filled round (all of them at
+// small M) each split into P parts along K so that about one item runs per SM (at most 16
+// parts, at least one stage each).  P = 1 (F = ntiles) when splitting gains nothing.
+QmmSplit qmm_split_plan(int M, int N, int K) {
   using namespace tc;
   const int ntiles = ((M + BN - 1) / BN) * ((N + BM - 1) / BM);
   const int nks = (K + BK - 1) / BK;
-  int P = num_sms() / ntiles;
+  const int sms = num_sms();
+  QmmSplit sp;
+  sp.ntiles = ntiles;
+  sp.F = ntiles / sms * sms;
+  const int tail = ntiles - sp.F;
+  int P = tail > 0 ? sms / tail : 1;
   if (P > nks) P = nks;
   if (P > 16) P = 16;
-  return P < 2 ? 1 : P;
+  if (P < 2) {
+    sp.F = ntiles;
+    P = 1;
+  }
+  sp.P = P;
+  sp.part_bytes = P > 1 ? (size_t)(ntiles - sp.F) * P * BM * BN * sizeof(float) : 0;
+  return sp;
 }
 
 int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, const uint2* prm, const uint32_t* w,
-                  __nv_bfloat16* y, int M, int N, int K, int P, float* part, cudaStream_t stream) {
+                  __nv_bfloat16* y, int M, int N, int K, const QmmSplit& sp, float* part, cudaStream_t stream) {
   using namespace tc;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(QVX_ERR_CUDA, "qvx_qmm: cuTensorMapEncodeTiled unavailable");
@@ -530,9 +555,9 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
   if (r != CUDA_SUCCESS) return fail(QVX_ERR_CUDA, "qvx_qmm: w tensor map encode failed (%d)", (int)r);
   // y [M, N] bf16 written by 256 x 128 TMA stores (clipped at the edges) when its rows are
   // 16-byte multiples; otherwise the epilogue stores elements directly
-  if (P > 1 && !part) return fail(QVX_ERR_INVALID, "qvx_qmm: K parts need a partial-sum buffer");
-  if (P < 1) P = 1;
-  const bool staged = P == 1 && (N % 8 == 0) && aligned(y, 16);
+  if (sp.P > 1 && !part) return fail(QVX_ERR_INVALID, "qvx_qmm: K parts need a partial-sum buffer");
+  const int F = sp.P > 1 ? sp.F : sp.ntiles, P = sp.P > 1 ? sp.P : 1;
+  const bool staged = (N % 8 == 0) && aligned(y, 16);
   CUtensorMap tmap_y;
   memset(&tmap_y, 0, sizeof(tmap_y));
   if (staged) {
@@ -553,16 +578,17 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
       return fail(QVX_ERR_CUDA, "qvx_qmm: cannot set shared memory size");
     if (dev >= 0 && dev < 64) attr_set[dev][staged] = true;
   }
-  const int nitems = ((M + BN - 1) / BN) * ((N + BM - 1) / BM) * P;
+  const int nitems = F + (sp.ntiles - F) * P;
   const int grid = nitems < num_sms() ? nitems : num_sms();
-  kern<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap_x, tmap_w, tmap_y, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N), P,
+  kern<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap_x, tmap_w, tmap_y, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N), F, P,
                                              P > 1 ? part : nullptr, status);
   int rc = check_launch("qvx_qmm");
   if (rc || P == 1) return rc;
-  const long long mn = (long long)M * N;
-  long long blocks = (mn + 255) / 256;
+  const int ntail = sp.ntiles - F;
+  const long long total = (long long)ntail * BM * BN;
+  long long blocks = (total + 255) / 256;
   if (blocks > (long long)num_sms() * 8) blocks = (long long)num_sms() * 8;
-  qmm_split_sum_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part, y, P, mn);
+  qmm_tail_sum_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part, y, M, N, F, P, ntail);
   return check_launch("qvx_qmm K-part sum");
 }
 
