@@ -163,6 +163,12 @@ def measure_configs(torch, device, hbm_peak, tc_peak):
     out["qk_condition_B8_T2048"] = {"ms": round(ms, 4), "gbs": round(qkb / ms / 1e6, 1),
                                     "frac_hbm": round(qkb / ms / 1e6 / hbm_peak, 3)}
     del qk
+    # sampling after lm_head (engine/sampler.py defaults: T 0.6, top_p 0.95, top_k 20) on a
+    # bf16 logits row of the Qwen vocabulary: scores + pick, one token
+    logits = (torch.randn((1, 248320), device=device, generator=g) * 3).to(torch.bfloat16)
+    ms = _cuda_time(torch, lambda: qvex.sample_pick(qvex.sample_scores(logits), greedy=False, seed=1, offset=1), 20)
+    out["sampler_V248320"] = {"ms": round(ms, 4), "tokens_per_s": round(1e3 / ms, 1)}
+    del logits
     # gated DeltaNet: decode step (HBM: state in + out) and 2048-step prefill (serial in T)
     for B, T in ((1, 1), (8, 1), (1, 2048), (8, 2048)):
         args = gd_case(torch, device, B, T)

@@ -193,6 +193,28 @@ int qvx_gated_delta(const void* q, const void* k, const void* v, const void* a, 
                     float* state_out, float* state_mid, int B, int T, int Hk, int Hv, int Dk,
                     int Dv, void* stream);
 
+/* ---------------------------------------------------------------- sampling */
+
+/* Replaces Sampler.scores (engine/sampler.py:30-62) for M rows of V logits (bf16 when
+ * logits_dtype == 0, fp32 when 1): l = (logit - presence_penalty * seen) / temperature;
+ * the top_k largest values sorted descending are the candidates; with 0 < top_p < 1 the
+ * cutoff is the smallest candidate whose softmax mass before it is < top_p, else the
+ * k-th largest; scores = l - logsumexp(l over l >= cutoff), -inf below the cutoff.
+ * temperature <= 0 (greedy): scores = the penalised logits.  seen (fp32 [V], 0 or 1) may
+ * be NULL.  top_k in 1..1024, or outside 1..V-1 for the whole vocabulary (then only
+ * without top_p).  scores fp32 [M, V]. */
+int qvx_sample_scores(const void* logits, int logits_dtype, const float* seen, float* scores, int M,
+                      int V, float temperature, float top_p, int top_k, float presence_penalty,
+                      void* stream);
+
+/* Replaces Sampler.pick (engine/sampler.py:63-64): tokens[m] = argmax of row m (the first
+ * index of the largest score) when greedy, else a draw from softmax(row) by the
+ * Gumbel-max trick with a counter-based generator keyed by (seed, offset, row); the
+ * reference's mx.random.categorical stream cannot be reproduced, so draws agree with it
+ * in distribution only.  scores fp32 [M, V], tokens int32 [M]. */
+int qvx_sample_pick(const float* scores, int32_t* tokens, int M, int V, int greedy,
+                    unsigned long long seed, unsigned long long offset, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,6 +48,8 @@ def lib():
         L.orc_gated_delta.argtypes = [P] * 11 + [I] * 6
         L.orc_gated_delta.restype = I
         L.orc_qk_condition.argtypes = [P, P, I64, I]
+        L.orc_sample_scores.argtypes = [P, P, P, I64, I64, ctypes.c_float, ctypes.c_float, I, ctypes.c_float]
+        L.orc_sample_scores.restype = I
         L.orc_f32_to_bf16.argtypes = [P, P, I64]
         L.orc_bf16_to_f32.argtypes = [P, P, I64]
         L.orc_num_threads.restype = I
@@ -195,6 +197,21 @@ def qk_condition(q, k):
     D = q.shape[-1]
     lib().orc_qk_condition(_p(q), _p(k), q.size // D, D)
     return q, k
+
+
+def sample_scores(logits, seen=None, temperature=0.6, top_p=0.95, top_k=20, presence_penalty=0.0):
+    """engine/sampler.py:30-62 (Sampler.scores) on fp32 logits [M, V]; seen [V] or None."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    if x.ndim == 1:
+        x = x[None]
+    M, V = x.shape
+    out = np.empty_like(x)
+    sn = None if seen is None else np.ascontiguousarray(seen, dtype=np.float32)
+    rc = lib().orc_sample_scores(_p(x), _p(sn) if sn is not None else None, _p(out), M, V, temperature, top_p,
+                                 top_k, presence_penalty)
+    if rc:
+        raise MemoryError("oracle sample_scores")
+    return out
 
 
 def threads_env() -> int:

@@ -42,6 +42,10 @@
  *                             elements [l*Dk/32, (l+1)*Dk/32) of each row.
  *   orc_qk_condition          engine/model.py:275-277: q <- Dk^-1 * rms_norm(q),
  *                             k <- Dk^-1/2 * rms_norm(k), eps 1e-6, no weight.
+ *   orc_sample_scores         engine/sampler.py:30-62 (Sampler.scores): presence
+ *                             penalty, temperature, top-k candidates sorted
+ *                             descending, top-p cutoff (keep while cumsum - prob <
+ *                             top_p), mask below the cutoff, log-softmax; fp32.
  *
  * Build: oracle/Makefile (gcc -O3 -fopenmp -ffp-contract=off; IEEE arithmetic,
  * no fast-math, so the integer/byte paths are bit-exact with the kernels).
@@ -361,4 +365,62 @@ void orc_qk_condition(uint16_t* q, uint16_t* k, int64_t rows, int D) {
       for (int i = 0; i < D; ++i) p[i] = f2bf(sc * bf2f(f2bf(bf2f(p[i]) * rn)));
     }
   }
+}
+
+/* ---------------------------------------------------------------- sampler scores */
+
+static int cmp_desc(const void* a, const void* b) {
+  const float x = *(const float*)a, y = *(const float*)b;
+  return (x < y) - (x > y);
+}
+
+/* engine/sampler.py:30-62 for M rows of V fp32 logits.  seen (V floats, 0 or 1) may be
+ * NULL.  temperature <= 0 is greedy: the penalised logits come back unchanged.  top_k
+ * outside 1..V-1 means the whole vocabulary is the candidate set.  Returns 0. */
+int orc_sample_scores(const float* logits, const float* seen, float* out, int64_t M, int64_t V,
+                      float temperature, float top_p, int top_k, float presence_penalty) {
+  float* cand = (float*)malloc(sizeof(float) * (size_t)V);
+  float* l = (float*)malloc(sizeof(float) * (size_t)V);
+  if (!cand || !l) { free(cand); free(l); return -1; }
+  for (int64_t m = 0; m < M; ++m) {
+    const float* x = logits + m * V;
+    float* o = out + m * V;
+    for (int64_t i = 0; i < V; ++i) {
+      float v = x[i];
+      if (seen && presence_penalty != 0.0f) v = v - presence_penalty * seen[i];
+      l[i] = v;
+    }
+    if (temperature <= 0.0f) {
+      memcpy(o, l, sizeof(float) * (size_t)V);
+      continue;
+    }
+    for (int64_t i = 0; i < V; ++i) l[i] = l[i] / temperature;
+    memcpy(cand, l, sizeof(float) * (size_t)V);
+    qsort(cand, (size_t)V, sizeof(float), cmp_desc);
+    const int64_t nc = (top_k > 0 && top_k < V) ? top_k : V;
+    float cutoff = cand[nc - 1];
+    if (top_p > 0.0f && top_p < 1.0f) {
+      /* mx.softmax(cand), mx.cumsum(probs) - probs < top_p, min over the kept */
+      const float mx = cand[0];
+      float sum = 0.0f;
+      for (int64_t i = 0; i < nc; ++i) sum += expf(cand[i] - mx);
+      float cum = 0.0f, best = INFINITY;
+      for (int64_t i = 0; i < nc; ++i) {
+        const float p = expf(cand[i] - mx) / sum;
+        cum += p;
+        if (cum - p < top_p && cand[i] < best) best = cand[i];
+      }
+      cutoff = best;
+    }
+    /* mx.logsumexp over the masked logits: max + log(sum exp(l - max)) */
+    const float mx = cand[0];
+    float s = 0.0f;
+    for (int64_t i = 0; i < V; ++i)
+      if (l[i] >= cutoff) s += expf(l[i] - mx);
+    const float lse = mx + logf(s);
+    for (int64_t i = 0; i < V; ++i) o[i] = l[i] >= cutoff ? l[i] - lse : -INFINITY;
+  }
+  free(cand);
+  free(l);
+  return 0;
 }

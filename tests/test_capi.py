@@ -159,6 +159,21 @@ def test_qmv_allgather_rejects_bad_descriptors(L):
     assert ctypes.sizeof(_lib.QvxGather) == 160  # 8 + 8 pointers, epoch, 5 ints (+4 padding)
 
 
+def test_sampler_rejects(L):
+    F = ctypes.c_float
+    # M, V, dtype
+    assert L.qvx_sample_scores(DUMMY, 2, None, DUMMY, 1, 100, F(0.6), F(0.95), 20, F(0), None) == 1
+    assert L.qvx_sample_scores(DUMMY, 0, None, DUMMY, 1, 0, F(0.6), F(0.95), 20, F(0), None) == 1
+    assert L.qvx_sample_scores(None, 0, None, DUMMY, 1, 100, F(0.6), F(0.95), 20, F(0), None) == 1
+    assert L.qvx_sample_scores(P(4097), 1, None, DUMMY, 1, 100, F(0.6), F(0.95), 20, F(0), None) == 3
+    # top_k beyond the supported candidate count, and top_p over the whole vocabulary
+    assert L.qvx_sample_scores(DUMMY, 0, None, DUMMY, 1, 5000, F(0.6), F(0.95), 2000, F(0), None) == 2
+    assert L.qvx_sample_scores(DUMMY, 0, None, DUMMY, 1, 5000, F(0.6), F(0.95), 0, F(0), None) == 2
+    assert L.qvx_sample_scores(DUMMY, 0, None, DUMMY, 0, 5000, F(0.6), F(0.95), 20, F(0), None) == 0
+    assert L.qvx_sample_pick(None, DUMMY, 1, 100, 1, 0, 0, None) == 1
+    assert L.qvx_sample_pick(DUMMY, DUMMY, 1, 0, 1, 0, 0, None) == 1
+
+
 def test_qk_condition_rejects(L):
     assert L.qvx_qk_condition(DUMMY, DUMMY, DUMMY, DUMMY, 8, 127, None) == 1   # odd D
     assert L.qvx_qk_condition(DUMMY, DUMMY, DUMMY, DUMMY, 8, 258, None) == 1   # D > 256

@@ -1,0 +1,114 @@
+"""Sampler.scores / Sampler.pick (engine/sampler.py:30-64) on the GPU against the CPU
+restatement.  The kept set (finite scores) must match exactly; kept scores within 2e-5
+(the kernel's sums run in a tree, the oracle's in index order).  Greedy picks are the
+first index of the maximum; sampled picks land only on kept tokens and follow softmax of
+the scores in distribution.
+"""
+import numpy as np
+import pytest
+import torch
+
+import detrand
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SCORE_ATOL = 2e-5
+
+
+@pytest.fixture(scope="module")
+def qvex():
+    import qvex as q
+    from qvex.build import build
+    build()
+    q.load_library()
+    return q
+
+
+def _logits(M, V, seed, scale=3.0):
+    return (detrand.normal((M, V), seed) * scale).astype(np.float32)
+
+
+def _check(got, ref):
+    gk, rk = np.isfinite(got), np.isfinite(ref)
+    assert np.array_equal(gk, rk)
+    assert np.all(got[~gk] == -np.inf)
+    assert np.max(np.abs(got[gk] - ref[rk])) <= SCORE_ATOL
+
+
+@pytest.mark.parametrize("M,V,T,top_p,top_k", [
+    (1, 248320, 0.6, 0.95, 20),      # the reference's defaults at the Qwen vocabulary
+    (3, 5000, 1.0, 0.5, 64),
+    (2, 1000, 0.8, 1.0, 1024),       # top-k only
+    (1, 333, 0.7, 0.9, 1),
+    (2, 777, 1.3, 0.0, 0),           # whole vocabulary, no top-p: a log-softmax
+])
+def test_scores_match_oracle_fp32(qvex, M, V, T, top_p, top_k):
+    x = _logits(M, V, 100 + V)
+    ref = O.sample_scores(x, None, T, top_p, top_k, 0.0)
+    got = qvex.sample_scores(torch.from_numpy(x).cuda(), T, top_p, top_k).cpu().numpy()
+    _check(got, ref)
+
+
+def test_scores_bf16_logits_ties_and_penalty(qvex):
+    """bf16 logits (many exact ties at the k-th value) with a presence penalty."""
+    M, V = 2, 20000
+    xb = O.f32_to_bf16(_logits(M, V, 7, scale=2.0))
+    x32 = O.bf16_to_f32(xb)
+    seen = np.zeros(V, np.float32)
+    seen[detrand.integers((300,), 8, V)] = 1.0
+    ref = O.sample_scores(x32, seen, 0.6, 0.95, 20, 0.7)
+    xt = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+    got = qvex.sample_scores(xt, 0.6, 0.95, 20, 0.7, torch.from_numpy(seen).cuda()).cpu().numpy()
+    _check(got, ref)
+
+
+def test_greedy_scores_and_pick(qvex):
+    M, V = 4, 50000
+    x = _logits(M, V, 11)
+    x[1, 123] = x[1, 4567] = x[1].max() + 1.0   # a tie: the first index wins
+    seen = np.zeros(V, np.float32)
+    seen[[5, 6]] = 1.0
+    ref = O.sample_scores(x, seen, 0.0, 0.95, 20, 0.5)
+    s = qvex.sample_scores(torch.from_numpy(x).cuda(), 0.0, 0.95, 20, 0.5, torch.from_numpy(seen).cuda())
+    np.testing.assert_array_equal(s.cpu().numpy(), ref)
+    tok = qvex.sample_pick(s, greedy=True).cpu().numpy()
+    np.testing.assert_array_equal(tok, np.argmax(ref, axis=1))
+    assert tok[1] == 123
+
+
+def test_sampled_picks_follow_the_distribution(qvex):
+    """4096 rows of the same scores draw 4096 independent tokens: all kept, frequencies
+    within a few standard errors of softmax(scores)."""
+    V = 3000
+    x = _logits(1, V, 21, scale=1.0)
+    s1 = qvex.sample_scores(torch.from_numpy(x).cuda(), 0.9, 0.8, 16)
+    rows = 4096
+    s = s1.expand(rows, V).contiguous()
+    tok = qvex.sample_pick(s, greedy=False, seed=1234, offset=1).cpu().numpy()
+    p = np.exp(s1.cpu().numpy()[0].astype(np.float64))
+    kept = np.flatnonzero(p > 0)
+    assert np.isin(tok, kept).all()
+    freq = np.bincount(tok, minlength=V)[kept] / rows
+    se = np.sqrt(p[kept] * (1 - p[kept]) / rows)
+    assert np.all(np.abs(freq - p[kept]) <= 5 * se + 1e-3)
+    # another offset draws differently, the same offset repeats
+    again = qvex.sample_pick(s, greedy=False, seed=1234, offset=1).cpu().numpy()
+    other = qvex.sample_pick(s, greedy=False, seed=1234, offset=2).cpu().numpy()
+    assert np.array_equal(tok, again) and not np.array_equal(tok, other)
+
+
+def test_sampler_class_mirrors_reference(qvex):
+    """Sampler(SamplingParams(...)) end to end: presence penalty through observe()."""
+    from qvex.sampler import Sampler, SamplingParams
+    V = 4000
+    x = torch.from_numpy(_logits(1, V, 31)).cuda()
+    smp = Sampler(SamplingParams(temperature=0.0, presence_penalty=100.0, seed=5), V)
+    first = int(smp.pick(smp.scores(x))[0])
+    smp.observe(torch.tensor([first], device="cuda"))
+    second = int(smp.pick(smp.scores(x))[0])
+    assert second != first      # the penalty pushes the seen token down
+    smp2 = Sampler(SamplingParams(seed=9), V)
+    t = smp2.pick(smp2.scores(x))
+    sc = smp2.scores(x)
+    assert torch.isfinite(sc[0, t[0].long()])
