@@ -1,10 +1,12 @@
 // Token sampling after the lm_head projection: Sampler.scores and Sampler.pick
 // (engine/sampler.py:30-62).
 //
-// scores, one CTA of 1024 threads per row of V logits (bf16 or fp32):
+// scores, per row of V logits (bf16 or fp32) -- one cluster of 8 CTAs per row when the
+// candidate bound below allows (the usual case), else one CTA of 1024 threads:
 //   1. l = (logit - presence_penalty * seen) / temperature, written to `scores` (fp32).
 //      temperature <= 0 is greedy: the penalised logits are the scores, nothing else.
-//   2. The top_k candidates (top_k <= 1024): radix select of the k-th largest value on
+//   2. The top_k candidates (top_k <= 1024; the cluster path's selection is described at
+//      its kernel): radix select of the k-th largest value on
 //      order-preserving 32-bit keys, 8 bits per pass (four passes over the row, per-warp
 //      histograms in shared memory), then the values above it plus copies of it, sorted
 //      descending by a bitonic sort in shared memory -- the same multiset of values the
@@ -17,11 +19,14 @@
 // bit for bit.  The whole vocabulary as the candidate set (top_k outside 1..V-1) is
 // supported without top_p (a plain log-softmax).
 //
-// pick: argmax per row (greedy: the first index of the largest score), or a draw from
+// pick (one cluster of 8 CTAs per row): argmax per row (greedy: the first index of the
+// largest score), or a draw from
 // softmax(scores) by the Gumbel-max trick, argmax(scores + G) with G = -log(-log(u)) and
 // u from the SplitMix64 mixer (Steele, Lea and Flood, 2014) of (seed, offset, row, index):
 // the reference draws with mx.random.categorical, whose random stream cannot be matched,
 // so sampling agrees in distribution only.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace qvx {
@@ -216,6 +221,166 @@ __global__ void __launch_bounds__(kSmpThreads, 1)
   }
 }
 
+// Bitonic sort, descending, of n (a power of two <= 8192) floats in shared memory by the
+// whole block.
+__device__ void bitonic_desc(float* a, int n) {
+  for (int size = 2; size <= n; size <<= 1)
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        const int j = t ^ stride;
+        if (j > t) {
+          const float x = a[t], y = a[j];
+          if (((t & size) == 0) ? (x < y) : (x > y)) {
+            a[t] = y;
+            a[j] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+}
+
+__device__ __forceinline__ int pow2_at_least(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+// scores with one cluster of kSmpCluster CTAs per row (rank r takes elements
+// [r S, (r+1) S)), talking through distributed shared memory.  Candidates without radix
+// passes: every thread keeps the maximum of its own elements; the k-th largest of all
+// threads' maxima, tau, is a lower bound on the row's k-th largest value (k distinct
+// elements reach it).  Only elements above tau are collected (into rank 0): if fewer than
+// k, the rest of the top k are copies of tau.  A thread whose maximum exceeds tau holds
+// at most per_thread of them and fewer than k threads do, so at most k * per_thread
+// candidates: the host takes this path only when that fits kSmpCandCap.
+constexpr int kSmpCluster = 8;
+constexpr int kSmpCandCap = 4096;
+
+struct SmpClusterShared {
+  float maxima[kSmpThreads];
+  float big[2 * kSmpCandCap];  // rank 0: the ranks' top maxima, then the candidates
+  float red[kSmpWarps];
+  float part;                  // this rank's exp sum
+  float tau, mx, cutoff, lse;  // rank 0 broadcasts these
+  int count;
+};
+
+__global__ void __cluster_dims__(kSmpCluster, 1, 1) __launch_bounds__(kSmpThreads, 1)
+    sample_scores_cluster_kernel(const void* __restrict__ logits, int bf16, const float* __restrict__ seen,
+                                 float* __restrict__ scores, int V, float temperature, float top_p, int top_k,
+                                 float presence_penalty) {
+  __shared__ SmpClusterShared sh;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int tid = threadIdx.x;
+  const unsigned rank = cl.block_rank();
+  const size_t row = blockIdx.x / kSmpCluster;
+  const int S = (V + kSmpCluster - 1) / kSmpCluster;
+  const int e0 = (int)rank * S, e1 = min(V, e0 + S);
+  float* l = scores + row * (size_t)V;
+  const bool greedy = !(temperature > 0.0f);
+  const bool penal = seen != nullptr && presence_penalty != 0.0f;
+
+  // 1. penalised, tempered logits; each thread's maximum
+  float mt = -INFINITY;
+  for (int i = e0 + tid; i < e1; i += kSmpThreads) {
+    float v = bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(logits)[row * (size_t)V + i])
+                   : static_cast<const float*>(logits)[row * (size_t)V + i];
+    if (penal) v = __fsub_rn(v, __fmul_rn(presence_penalty, seen[i]));
+    if (!greedy) v = __fdiv_rn(v, temperature);
+    l[i] = v;
+    mt = fmaxf(mt, v);
+  }
+  if (greedy) return;  // every CTA of the cluster returns here
+  const int k = (top_k > 0 && top_k < V) ? top_k : 0;  // 0: the whole vocabulary
+  SmpClusterShared* root = cl.map_shared_rank(&sh, 0);
+
+  // 2. this rank's k largest thread maxima (all of them sorted), to rank 0
+  sh.maxima[tid] = mt;
+  if (tid == 0) sh.count = 0;
+  __syncthreads();
+  bitonic_desc(sh.maxima, kSmpThreads);
+  const int kk = k > 0 ? k : 1;  // the whole vocabulary only needs the maximum
+  const int nm = pow2_at_least(kSmpCluster * kk);
+  cl.sync();
+  for (int i = tid; i < kk; i += kSmpThreads) root->big[rank * kk + i] = sh.maxima[i];
+  cl.sync();
+  if (rank == 0) {
+    for (int i = kSmpCluster * kk + tid; i < nm; i += kSmpThreads) sh.big[i] = -INFINITY;
+    __syncthreads();
+    bitonic_desc(sh.big, nm);
+    if (tid == 0) {
+      sh.mx = sh.big[0];
+      sh.tau = sh.big[kk - 1];
+    }
+  }
+  cl.sync();
+  const float mx = root->mx, tau = root->tau;
+
+  // 3. candidates above tau, sorted, top k; then top_p
+  float cutoff = -INFINITY;
+  if (k > 0) {
+    for (int i = e0 + tid; i < e1; i += kSmpThreads) {
+      const float v = l[i];
+      if (v > tau) root->big[atomicAdd(&root->count, 1)] = v;
+    }
+    cl.sync();
+    if (rank == 0) {
+      const int c = sh.count;  // < k * per_thread <= kSmpCandCap, checked on the host
+      const int n = pow2_at_least(c > k ? c : k);
+      for (int i = c + tid; i < n; i += kSmpThreads) sh.big[i] = i < k ? tau : -INFINITY;
+      __syncthreads();
+      bitonic_desc(sh.big, n);  // the top k of the row are big[0 .. k-1]
+      float cut = sh.big[k - 1];
+      if (top_p > 0.0f && top_p < 1.0f) {
+        float keepmin = INFINITY;
+        // softmax over the k candidates, inclusive prefix sum, keep while cumsum - p < top_p
+        float sum = 0.0f;
+        for (int base = 0; base < k; base += kSmpThreads) {
+          const int i = base + tid;
+          sum += block_sum(i < k ? expf(sh.big[i] - mx) : 0.0f, sh.red);
+        }
+        float carry = 0.0f;
+        for (int base = 0; base < k; base += kSmpThreads) {
+          const int i = base + tid;
+          const float c2 = i < k ? sh.big[i] : -INFINITY;
+          const float p = i < k ? __fdiv_rn(expf(c2 - mx), sum) : 0.0f;
+          const float cum = carry + block_scan(p, sh.red);
+          if (i < k && __fsub_rn(cum, p) < top_p) keepmin = fminf(keepmin, c2);
+          carry = block_sum(p, sh.red) + carry;
+        }
+        cut = block_min(keepmin, sh.red);
+      }
+      if (tid == 0) sh.cutoff = cut;
+    }
+    cl.sync();
+    cutoff = root->cutoff;
+  }
+
+  // 4. log-softmax of the masked row: exp sums per rank, added by rank 0 in rank order
+  float s = 0.0f;
+  for (int i = e0 + tid; i < e1; i += kSmpThreads) {
+    const float v = l[i];
+    if (v >= cutoff) s += expf(v - mx);
+  }
+  s = block_sum(s, sh.red);
+  if (tid == 0) sh.part = s;
+  cl.sync();
+  if (rank == 0 && tid == 0) {
+    float t = 0.0f;
+    for (int r = 0; r < kSmpCluster; ++r) t += cl.map_shared_rank(&sh, r)->part;
+    sh.lse = mx + logf(t);
+  }
+  cl.sync();
+  const float lse = root->lse;
+  for (int i = e0 + tid; i < e1; i += kSmpThreads) {
+    const float v = l[i];
+    l[i] = v >= cutoff ? v - lse : -INFINITY;
+  }
+  cl.sync();  // rank 0's shared memory stays alive until every rank has read it
+}
+
 __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
   z += 0x9E3779B97F4A7C15ull;
   z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
@@ -223,55 +388,75 @@ __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
-__global__ void __launch_bounds__(kSmpThreads, 1)
+// pick with one cluster of kSmpCluster CTAs per row (rank r scans elements
+// [r S, (r+1) S)); rank 0 combines the ranks' (value, index) in rank order, so ties still
+// go to the first index.
+struct SmpPickShared {
+  float bv[kSmpWarps];
+  int bi[kSmpWarps];
+  float best;
+  int idx;
+};
+
+__device__ __forceinline__ void better(float& best, int& idx, float v, int i) {
+  if (v > best || (v == best && i < idx)) {
+    best = v;
+    idx = i;
+  }
+}
+
+__global__ void __cluster_dims__(kSmpCluster, 1, 1) __launch_bounds__(kSmpThreads, 1)
     sample_pick_kernel(const float* __restrict__ scores, int32_t* __restrict__ tokens, int V, int greedy,
                        unsigned long long seed, unsigned long long offset) {
-  __shared__ float bv[kSmpWarps];
-  __shared__ int bi[kSmpWarps];
+  __shared__ SmpPickShared sh;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const size_t row = blockIdx.x;
+  const unsigned rank = cl.block_rank();
+  const size_t row = blockIdx.x / kSmpCluster;
+  const int S = (V + kSmpCluster - 1) / kSmpCluster;
+  const int e0 = (int)rank * S, e1 = min(V, e0 + S);
   const float* s = scores + row * (size_t)V;
   const uint64_t stream = splitmix64(seed ^ splitmix64(offset ^ splitmix64(row)));
   float best = -INFINITY;
   int idx = V;  // ties and all -inf rows: the first index wins
-  for (int i = tid; i < V; i += kSmpThreads) {
+  for (int i = e0 + tid; i < e1; i += kSmpThreads) {
     float v = s[i];
     if (!greedy && v > -INFINITY) {
       const uint64_t h = splitmix64(stream + (uint64_t)i);
       const float u = ((float)(h >> 40) + 0.5f) * 0x1p-24f;  // in (0, 1)
       v += -logf(-logf(u));
     }
-    if (v > best || (v == best && i < idx)) {
-      best = v;
-      idx = i;
-    }
+    better(best, idx, v, i);
   }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ov > best || (ov == best && oi < idx)) {
-      best = ov;
-      idx = oi;
-    }
-  }
+  for (int o = 16; o > 0; o >>= 1)
+    better(best, idx, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, idx, o));
   if (lane == 0) {
-    bv[warp] = best;
-    bi[warp] = idx;
+    sh.bv[warp] = best;
+    sh.bi[warp] = idx;
   }
   __syncthreads();
   if (warp == 0) {
-    best = lane < kSmpWarps ? bv[lane] : -INFINITY;
-    idx = lane < kSmpWarps ? bi[lane] : V;
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-      if (ov > best || (ov == best && oi < idx)) {
-        best = ov;
-        idx = oi;
-      }
+    best = lane < kSmpWarps ? sh.bv[lane] : -INFINITY;
+    idx = lane < kSmpWarps ? sh.bi[lane] : V;
+    for (int o = 16; o > 0; o >>= 1)
+      better(best, idx, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, idx, o));
+    if (lane == 0) {
+      sh.best = best;
+      sh.idx = idx;
     }
-    if (lane == 0) tokens[row] = idx < V ? idx : 0;
   }
+  cl.sync();
+  if (rank == 0 && tid == 0) {
+    float b = -INFINITY;
+    int ix = V;
+    for (int r = 0; r < kSmpCluster; ++r) {
+      const SmpPickShared* o = cl.map_shared_rank(&sh, r);
+      better(b, ix, o->best, o->idx);
+    }
+    tokens[row] = ix < V ? ix : 0;
+  }
+  cl.sync();  // every rank's shared memory stays alive until rank 0 has read it
 }
 
 }  // namespace qvx
@@ -295,8 +480,17 @@ extern "C" int qvx_sample_scores(const void* logits, int logits_dtype, const flo
       return fail(QVX_ERR_UNSUPPORTED, "qvx_sample_scores: top_p over the whole vocabulary needs top_k in 1..%d",
                   kSmpMaxK);
   }
-  sample_scores_kernel<<<M, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      logits, logits_dtype == 0, seen, scores, V, temperature, top_p, top_k, presence_penalty);
+  // one cluster of CTAs per row when the candidate bound fits, else one CTA per row with
+  // radix selection
+  const int k = (top_k > 0 && top_k < V) ? top_k : 0;
+  const long long per_thread = ((long long)(V + kSmpCluster - 1) / kSmpCluster + kSmpThreads - 1) / kSmpThreads;
+  if ((long long)k * per_thread <= kSmpCandCap && k <= kSmpCandCap / kSmpCluster) {
+    sample_scores_cluster_kernel<<<M * kSmpCluster, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        logits, logits_dtype == 0, seen, scores, V, temperature, top_p, top_k, presence_penalty);
+  } else {
+    sample_scores_kernel<<<M, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        logits, logits_dtype == 0, seen, scores, V, temperature, top_p, top_k, presence_penalty);
+  }
   return check_launch("qvx_sample_scores");
 }
 
@@ -307,7 +501,7 @@ extern "C" int qvx_sample_pick(const float* scores, int32_t* tokens, int M, int 
   if (M == 0) return QVX_OK;
   if (!scores || !tokens) return fail(QVX_ERR_INVALID, "qvx_sample_pick: null pointer");
   if (!aligned(scores, 4) || !aligned(tokens, 4)) return fail(QVX_ERR_ALIGN, "qvx_sample_pick: misaligned buffer");
-  sample_pick_kernel<<<M, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(scores, tokens, V, greedy, seed,
-                                                                               offset);
+  sample_pick_kernel<<<M * kSmpCluster, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(scores, tokens, V,
+                                                                                              greedy, seed, offset);
   return check_launch("qvx_sample_pick");
 }

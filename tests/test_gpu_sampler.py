@@ -42,6 +42,7 @@ def _check(got, ref):
     (2, 1000, 0.8, 1.0, 1024),       # top-k only
     (1, 333, 0.7, 0.9, 1),
     (2, 777, 1.3, 0.0, 0),           # whole vocabulary, no top-p: a log-softmax
+    (1, 248320, 1.0, 0.9, 600),      # beyond the cluster path's candidate bound: one CTA per row
 ])
 def test_scores_match_oracle_fp32(qvex, M, V, T, top_p, top_k):
     x = _logits(M, V, 100 + V)
