@@ -519,7 +519,7 @@ def run_ours(args):
             "config": {"workload": "config 1: all 145 4-bit g64 linears of one Qwen3.5-9B-shaped decode step",
                        "M": M, "layers": args.layers, "weight_bytes_per_step": weight_bytes,
                        "parallelism": ("single GPU" if world == 1 else
-                                       f"column-shard x{world} + all-gather fused into the qmv kernel (NVLink peer stores)"
+                                       f"column-shard x{world} + all-gather fused into the qmv kernel (tagged inbox words over NVLink)"
                                        if fused else f"column-shard x{world} + NCCL all-gather"),
                        "l2": "inputs larger than L2 (4.46 GB of weights per step)", "cuda_graph": True},
             "tok_per_s": round(1000.0 / ms_step, 1),
