@@ -13,7 +13,9 @@
 // hide its handshakes: with K = 64 per stage the producer and MMA threads alone took
 // longer per stage than the tensor cores.  One CTA per SM, persistent over tiles; tile
 // t -> (weight block t / tiles_m, token block t % tiles_m), so CTAs running at the same
-// time share weight rows in L2 while x stays L2-resident.
+// time share weight rows in L2 while x stays L2-resident.  Tiles that would run in a last,
+// partly filled round (all tiles at small M) are split along K over the idle SMs; their
+// parts' fp32 partial sums are added by qmm_tail_sum_kernel (qmm_split_plan).
 //
 // One ring of S stages, each holding the stage's x tile (2 x 16 KB), code tile (16 KB)
 // and group multipliers (4 KB), filled by TMA (full[]) and released by ONE tcgen05
