@@ -235,8 +235,11 @@ class ShardedQLinear:
         self.out_features = sum(p.w.shape[0] for p in parts)
         self.peer = peer
         if peer is not None:
-            self.slot = peer.reserve()
             n_loc = self.local.w.shape[0]
+            if n_loc % 2:
+                raise ValueError(f"the fused gather moves rows in pairs: {n_loc} rows per rank is odd "
+                                 "(use the NCCL gather, peer=None)")
+            self.slot = peer.reserve()
             self._desc = peer.descriptor(self.slot, self.out_features, self.rank * n_loc)
 
     def __call__(self, x: torch.Tensor, *, gather: bool = True) -> torch.Tensor:

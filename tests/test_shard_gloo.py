@@ -155,3 +155,29 @@ def test_gather_descriptor_addresses():
         assert outs[slot] + 2 * 4096 <= inboxes[slot] and inboxes[slot] + 4 * 4096 <= nxt
 
 
+
+
+def test_sharded_qlinear_rejects_odd_rows_for_fused_gather():
+    """The fused gather moves rows in pairs, so an odd per-rank row count is refused when
+    the layer is built, before any slot is taken."""
+    import torch
+    from qvex.model import QLinear
+    from qvex.shard import ShardedQLinear
+
+    class Peer:
+        taken = 0
+
+        def reserve(self):
+            Peer.taken += 1
+            return 0
+
+        def descriptor(self, *a):
+            return None
+    lin = QLinear(torch.zeros(6, 8, dtype=torch.int32), torch.zeros(6, 1, dtype=torch.bfloat16),
+                  torch.zeros(6, 1, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="pairs"):
+        ShardedQLinear(lin, rank=0, world=2, peer=Peer())
+    assert Peer.taken == 0
+    ok = ShardedQLinear(QLinear(torch.zeros(8, 8, dtype=torch.int32), torch.zeros(8, 1, dtype=torch.bfloat16),
+                                torch.zeros(8, 1, dtype=torch.bfloat16)), rank=1, world=2, peer=Peer())
+    assert ok.local.w.shape[0] == 4 and Peer.taken == 1
