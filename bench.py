@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the QVex hot path on B200: 4-bit g64 qmv over one decode step.
 
-Workload (the configuration the headline metric is quoted on): every
+Workload (the decode-step case the headline metric is quoted on): every
 4-bit group-64 linear of one decode step of a Qwen3.5-9B-shaped model (24 gated-DeltaNet
 + 8 gated-attention layers, hidden 4096, MLP 12288, vocab 248320; 145 projections,
 4.464 GB of packed weights), applied to x bf16 [M, K] ~ N(0,1) with M = 1.  Weights are
@@ -87,7 +87,7 @@ def _cuda_time(torch, fn, reps, warm=3):
 
 
 def config_cases(torch, device, small=False):
-    """Inputs of BASELINE configs 2 (quantize + prefill qmm) and 3 (gated DeltaNet)."""
+    """Inputs of the quantize + prefill-qmm case (W ~ N(0, 0.02) [12288, 4096], x [2048, 4096])."""
     import qvex
     g = torch.Generator(device=device)
     g.manual_seed(0)
@@ -319,6 +319,38 @@ def build_weights(torch, shape, rank, world, device, seed=0):
     return lins
 
 
+def full_linear(torch, shape, index, device, seed=0):
+    """Projection `index` of build_weights, unsharded (the same seeded generator)."""
+    from qvex.model import QLinear
+    name, N, K = shape.decode_linears()[index]
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 100003 + index)
+    w = torch.randint(-2 ** 31, 2 ** 31, (N, K // 8), dtype=torch.int64, device=device, generator=g).to(torch.int32)
+    s = (torch.randn((N, K // 64), device=device, generator=g).abs() * 0.002).to(torch.bfloat16)
+    b = (-8.0 * s.float()).to(torch.bfloat16)
+    return QLinear(w, s, b, 64, 4)
+
+
+def gather_check(torch, shape, lins, xs, full_out, world, device):
+    """After the timed replays: every rank recomputes a small (first k_proj) and the largest
+    (lm_head) projection unsharded with the single-GPU kernel and compares its gathered
+    output bit for bit (a row's arithmetic does not depend on how the rows are split).
+    Returns "ok" or the first mismatch."""
+    names = [n for n, _, _, _ in lins]
+    picks = [next(i for i, n in enumerate(names) if n.endswith("k_proj")), len(lins) - 1]
+    for i in picks:
+        name, N, K, _ = lins[i]
+        ref = full_linear(torch, shape, i, device)(xs[K])
+        got = full_out[i]
+        got = got.reshape(ref.shape) if got.dim() == 2 else got.permute(1, 0, 2).reshape(ref.shape)
+        torch.cuda.synchronize()
+        if not torch.equal(got.view(torch.int16), ref.view(torch.int16)):
+            bad = int((got.view(torch.int16) != ref.view(torch.int16)).sum())
+            return f"{name}: {bad} of {ref.numel()} outputs differ"
+        del ref
+    return "ok"
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -482,6 +514,20 @@ def run_ours(args):
         e2e_s = float(t.item())
     e2e_val = bytes_full * e2e_steps / e2e_s / 1e9
 
+    # multi-GPU correctness: the gathered outputs of the last replay against the unsharded
+    # kernel on every rank, and the device status word (a bounded wait that gave up)
+    check = None
+    if world > 1:
+        graph_full.replay()
+        torch.cuda.synchronize()
+        verdict = gather_check(torch, shape, lins, xs, full_out, world, device)
+        status = qvex._lib.device_status(torch.cuda.current_stream().cuda_stream)
+        flags = [None] * world
+        dist.all_gather_object(flags, (verdict, status))
+        check = {"gather_check": "ok" if all(v == "ok" for v, _ in flags) else [v for v, _ in flags],
+                 "device_status": max(st for _, st in flags),
+                 "checked": "first k_proj and lm_head, bit for bit against the unsharded kernel, every rank"}
+
     extra = {}
     if not args.no_extra and world == 1:
         for m2 in (2, 4, 8):
@@ -535,6 +581,8 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if check:
+            rec.update(check)
         if configs:
             rec["configs"] = configs
         if cpu:

@@ -92,7 +92,8 @@ int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* bi
  * call shares the array, so calls that overlap on the GPU (other streams, other host
  * threads) race: order them.  Nothing in it needs clearing, since each call writes all
  * the scratch it reads.  The first call on each device looks up the array's address;
- * make it before any stream capture. */
+ * make it before any stream capture.  That address belongs to the device's primary
+ * context: after cudaDeviceReset on a device, do not call this entry point there again. */
 int qvx_qmm_noalloc(const void* x, const uint32_t* w, const void* scales, const void* biases,
                     void* y, int M, int N, int K, int group_size, int bits, void* stream);
 
@@ -103,11 +104,19 @@ int qvx_qmm_noalloc(const void* x, const uint32_t* w, const void* scales, const 
 /* Where the outputs of a column-sharded projection go.  Rank r owns rows
  * [r * N, (r + 1) * N) of an n_total = world * N row projection (N even).  out[rank] is
  * this rank's full output (bf16 [M, n_total], row stride n_total); inbox[r] is rank r's
- * receive area for this projection (64-bit words [M, n_total / 2], each two bf16 outputs
- * and a 32-bit launch tag), as mapped in the calling process (peer mappings such as CUDA
- * IPC for r != rank, reachable over NVLink).  epoch points to this rank's counters in
- * device memory, two words per slot.  Inboxes and counters start at zero.  slot names the
- * projection: two projections must not share one.  out[r] for r != rank is not used. */
+ * receive area for this projection (64-bit words [M, 2, n_total / 2], each two bf16
+ * outputs and a 32-bit launch tag; launch t of the slot uses half t % 2, so a peer one
+ * launch ahead never overwrites words still being read), as mapped in the calling process
+ * (peer mappings such as CUDA IPC for r != rank, reachable over NVLink).  epoch points to
+ * this rank's counters in device memory, two words per slot.  Inboxes and counters start
+ * at zero.  slot names the projection: two projections must not share one.  out[r] for
+ * r != rank is not used.
+ *
+ * The ranks' launch counters of a slot advance in step only while every rank makes every
+ * call.  After a call that failed or timed out on any rank (or that one rank skipped), all
+ * ranks must stop, synchronise their devices, meet at a host barrier, zero their inboxes
+ * and counters (cudaMemset), synchronise again and meet at a second barrier before the
+ * next call; qvex.shard.PeerGather.reset() does exactly this. */
 typedef struct qvx_gather {
   void* out[QVX_MAX_RANKS];
   void* inbox[QVX_MAX_RANKS];

@@ -2,6 +2,8 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace qvx {
@@ -9,15 +11,19 @@ namespace qvx {
 __device__ int g_device_status = 0;
 
 int* device_status_ptr() {
-  static int* cache[64] = {};
+  // one atomic word per device index: concurrent first calls from several host threads
+  // each store the same address
+  static std::atomic<int*> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!cache[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<int*>(p);
+  int* p = cache[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void* a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_device_status) != cudaSuccess) return nullptr;
+    p = static_cast<int*>(a);
+    cache[dev].store(p, std::memory_order_release);
   }
-  return cache[dev];
+  return p;
 }
 
 static thread_local char t_last_error[512] = "";

@@ -25,6 +25,8 @@
 // Set-up: the first call on each device looks up the array's device address with
 // cudaGetSymbolAddress, with that device current, and keeps it for later calls.  Make
 // that first call before any stream capture begins.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace qvx {
@@ -41,22 +43,27 @@ constexpr size_t kQmmScratchBytes = size_t(16) << 20;
 // device address: kernels get the address from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_qmm_scratch[kQmmScratchBytes];
 
-// Device address of g_qmm_scratch on the current device, looked up once per device.
+// Device address of g_qmm_scratch on the current device, looked up once per device.  The
+// cache is one atomic word per device index, so first calls made at the same time from
+// several host threads are well defined (each stores the same address).  The address
+// belongs to the device's primary context: after cudaDeviceReset the library's module is
+// loaded again and the cached address is stale, so a process that resets a device must not
+// call qvx_qmm_noalloc on it afterwards.
 static int qmm_scratch_ptr(void** out) {
-  static void* cache[64] = {};
+  static std::atomic<void*> cache[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(QVX_ERR_CUDA, "qvx_qmm_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(QVX_ERR_UNSUPPORTED, "qvx_qmm_noalloc: device index %d beyond 63", dev);
-  if (!cache[dev]) {
-    void* p = nullptr;
+  void* p = cache[dev].load(std::memory_order_acquire);
+  if (!p) {
     e = cudaGetSymbolAddress(&p, g_qmm_scratch);
     if (e != cudaSuccess || !p)
       return fail(QVX_ERR_CUDA, "qvx_qmm_noalloc: cannot get the scratch address on device %d: %s", dev,
                   cudaGetErrorString(e));
-    cache[dev] = p;
+    cache[dev].store(p, std::memory_order_release);
   }
-  *out = cache[dev];
+  *out = p;
   return QVX_OK;
 }
 

@@ -364,18 +364,28 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       // their tags show this launch.  The tag is the slot's launch count + 1, read after
       // griddepcontrol.wait; the launch's last CTA advances it.  Also after an abort, so
       // that the peers do not wait out their timeout for this rank.
+      //
+      // Each token row of an inbox has two halves, and launch t uses half t & 1.  A peer
+      // finishes launch t once this rank's words of launch t have reached it, which does
+      // not mean that this rank has read the peer's words of launch t yet.  So the peer's
+      // launch t + 1 may store while this rank is still reading: it stores into the other
+      // half.  The peer cannot get to launch t + 2, which would use this half again,
+      // before it has received this rank's words of launch t + 1, and this rank sends
+      // those only after its launch t has completed (its gather starts after
+      // griddepcontrol.wait), that is, after it has read every word of launch t.
       pdl_wait();
       __syncwarp();
       const unsigned tag = *reinterpret_cast<volatile unsigned*>(g.epoch + 2 * g.slot) + 1u;
       const int p0 = r_begin >> 1, p1 = r_end >> 1;  // this CTA's row pairs
-      const size_t nh = (size_t)(g.n_total >> 1);     // pairs per token row
+      const size_t nh = (size_t)(g.n_total >> 1);     // pairs per token row (one inbox half)
+      const size_t half = (size_t)(tag & 1u);
       for (int m = 0; m < mc; ++m) {
         const uint32_t* own = reinterpret_cast<const uint32_t*>(g.out[g.rank] + (size_t)(m0 + m) * g.n_total);
         for (int j = p0 + lane; j < p1; j += 32) {
           const size_t pair = (size_t)(g.row0 >> 1) + j;
           const unsigned long long word = (unsigned long long)own[pair] | ((unsigned long long)tag << 32);
           for (int q = 0; q < g.world; ++q)
-            if (q != g.rank) st_relaxed_sys_u64(g.inbox[q] + (size_t)(m0 + m) * nh + pair, word);
+            if (q != g.rank) st_relaxed_sys_u64(g.inbox[q] + ((size_t)(m0 + m) * 2 + half) * nh + pair, word);
         }
       }
       const unsigned long long t0 = globaltimer_ns();
@@ -386,7 +396,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
           uint32_t* dst = reinterpret_cast<uint32_t*>(g.out[g.rank] + (size_t)(m0 + m) * g.n_total);
           for (int j = p0 + lane; j < p1 && !late; j += 32) {
             const size_t pair = (size_t)(q * N >> 1) + j;  // shards are equal: peer q starts at q N
-            const unsigned long long* src = g.inbox[g.rank] + (size_t)(m0 + m) * nh + pair;
+            const unsigned long long* src = g.inbox[g.rank] + ((size_t)(m0 + m) * 2 + half) * nh + pair;
             unsigned long long word = ld_relaxed_sys_u64(src);
             for (uint32_t it = 1; (unsigned)(word >> 32) != tag; ++it) {
               if ((it & 63) == 0 && (globaltimer_ns() - t0 > kWaitTimeoutNs || it > kWaitMaxPolls)) {

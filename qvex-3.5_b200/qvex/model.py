@@ -12,7 +12,8 @@ from .core import dequantize_rows, quantized_matmul
 
 
 class QLinear:
-    """Affine-quantized linear layer (y = x @ W^T)."""
+    """A projection whose weight is kept in the 4-bit affine group format; calling it
+    returns x times the transposed dequantised weight, computed by libqvex."""
 
     def __init__(self, w, scales, biases, group_size=64, bits=4):
         self.w, self.scales, self.biases = w, scales, biases
@@ -32,7 +33,8 @@ class QLinear:
 
     @staticmethod
     def fuse(layers: list["QLinear"]) -> "QLinear":
-        """Stack output rows of several layers sharing the same input (lossless)."""
+        """One layer whose output rows are those of ``layers`` in order, for projections that
+        read the same input: one launch then computes all of them, with identical results."""
         l0 = layers[0]
         if not all((l.group_size, l.bits) == (l0.group_size, l0.bits) for l in layers):
             raise AssertionError("fused layers must share the quantization (bits, group size)")
@@ -54,20 +56,21 @@ class QEmbedding:
 
 
 class RecurrentCache:
-    """Conv + SSM state of one gated-DeltaNet layer, with one-token rollback."""
+    """Per-layer decode state of a gated-DeltaNet layer (convolution window and recurrent
+    matrix) plus the copies needed to undo the newest token."""
 
     def __init__(self):
         self.conv = None   # [B, K-1, conv_dim]
         self.ssm = None    # [B, Hv, Dv, Dk] float32
         self.offset = 0
-        self.conv_prev = self.ssm_prev = None  # state one token back (speculative decoding)
+        self.conv_prev = self.ssm_prev = None  # states before the newest token, for a rejected draft
 
     def state(self):
         return [x for x in (self.conv, self.ssm) if x is not None]
 
     def rollback(self, n=1):
         if not (n == 1 and self.ssm_prev is not None):
-            raise AssertionError("can only roll back the last token")
+            raise AssertionError("rollback restores one token, and only once after a keep_prev step")
         self.conv, self.ssm = self.conv_prev, self.ssm_prev
         self.conv_prev = self.ssm_prev = None
         self.offset -= 1

@@ -77,7 +77,8 @@ class Sampler:
         return self.p.temperature <= 0
 
     def scores(self, logits: torch.Tensor, extra_seen: torch.Tensor | None = None) -> torch.Tensor:
-        """Full-vocab scores: penalised logits (greedy) or filtered log-probs (sampling)."""
+        """Scores over the whole vocabulary: the logits minus the presence penalty when greedy,
+        else log-probabilities restricted to the top-k / top-p set."""
         p = self.p
         seen = self.seen
         if seen is not None and extra_seen is not None:

@@ -51,6 +51,20 @@ def shard_fused(parts: list[QLinear], world: int, rank: int) -> QLinear:
     return QLinear.fuse([shard_linear(p, world, rank) for p in parts])
 
 
+def part_order(sizes: list[int], world: int, device=None) -> torch.Tensor:
+    """Column permutation from the rank-major order of a gathered fused projection (rank r's
+    block holds its shard of every part, in part order) to the order of the unsharded fused
+    projection (part j whole, then part j + 1): result[t] = gathered column of column t."""
+    per = [shard_rows(n, world, 0)[1] for n in sizes]
+    n_loc = sum(per)
+    idx = []
+    for j, pj in enumerate(per):
+        off = sum(per[:j])
+        for r in range(world):
+            idx.extend(range(r * n_loc + off, r * n_loc + off + pj))
+    return torch.tensor(idx, dtype=torch.long, device=device)
+
+
 def gather_columns(local_y: torch.Tensor, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
     """All-gather row shards: local_y [..., N/P] on every rank -> y [..., N] (rank-major).
 
@@ -81,9 +95,9 @@ GATHER_M_MAX = 8  # tokens a fused decode projection gathers (qvx_qmv's M <= 8)
 
 def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], list[int], int]:
     """Byte layout of one rank's PeerGather buffer: per slot, the full output (``region_bytes``
-    of bf16) and then its inbox (twice that: one 64-bit word, two outputs and a tag, per
-    output pair), each 256-byte aligned.  Returns the outputs' offsets, the inboxes'
-    offsets and the total size."""
+    of bf16) and then its inbox (four times that: one 64-bit word, two outputs and a tag,
+    per output pair, in two halves that alternating launches use), each 256-byte aligned.
+    Returns the outputs' offsets, the inboxes' offsets and the total size."""
     if any(b <= 0 for b in region_bytes):
         raise ValueError("every region needs a positive size")
 
@@ -96,7 +110,7 @@ def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], list[int], i
         outs.append(at)
         at = up(at + b)
         inboxes.append(at)
-        at = up(at + 2 * b)
+        at = up(at + 4 * b)
     return outs, inboxes, at
 
 
@@ -186,6 +200,20 @@ class PeerGather:
         arr = _DeviceArray(self.base[self.rank] + self.offsets[slot], (M, n_total))
         return torch.as_tensor(arr, device=f"cuda:{self.device}").view(torch.bfloat16)
 
+    def reset(self) -> None:
+        """Puts every slot back in its starting state: zero inboxes and launch counters on every
+        rank.  The ranks' counters of a slot stay in step only while every rank makes every
+        call, so after a call that failed, timed out (QvexTimeout, device status
+        QVX_ERR_TIMEOUT) or was skipped on any rank, every rank calls this before the next
+        gathered projection.  Collective: all ranks of the group must call it."""
+        rt = self._rt
+        _ck(rt.cudaDeviceSynchronize())
+        dist.barrier(self.group)   # no rank still stores into another's inbox
+        _ck(rt.cudaMemset(self._own, 0, self.nbytes))
+        self.epoch.zero_()
+        _ck(rt.cudaDeviceSynchronize())
+        dist.barrier(self.group)   # no rank starts a call while another still clears
+
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's (after a device sync and a
         barrier, so no rank still stores into it)."""
@@ -234,6 +262,11 @@ class ShardedQLinear:
         self.local = shard_fused(parts, self.world, self.rank)
         self.out_features = sum(p.w.shape[0] for p in parts)
         self.peer = peer
+        # Gathered rank by rank, the columns of a fused projection come out as
+        # [rank 0: part 0 shard, part 1 shard, ...][rank 1: ...]; _perm puts them back in the
+        # order of the unsharded QLinear.fuse(parts): [part 0][part 1]...
+        self._perm = part_order(
+            [p.w.shape[0] for p in parts], self.world, self.local.w.device) if len(parts) > 1 else None
         if peer is not None:
             n_loc = self.local.w.shape[0]
             if n_loc % 2:
@@ -243,10 +276,20 @@ class ShardedQLinear:
             self._desc = peer.descriptor(self.slot, self.out_features, self.rank * n_loc)
 
     def __call__(self, x: torch.Tensor, *, gather: bool = True) -> torch.Tensor:
+        """y = x @ W^T: all columns in the unsharded order (gather=True), or only this rank's
+        shard [part 0 shard | part 1 shard | ...] (gather=False)."""
         x2 = x.reshape(-1, x.shape[-1])
         if self.peer is not None and gather and x2.shape[0] <= GATHER_M_MAX:
             qmv_allgather(self.local, x2, self._desc)
-            return self.peer.output(self.slot, x2.shape[0], self.out_features).reshape(*x.shape[:-1],
-                                                                                        self.out_features)
+            y = self.peer.output(self.slot, x2.shape[0], self.out_features)
+            return self.in_part_order(y).reshape(*x.shape[:-1], self.out_features)
         y = self.local(x)
-        return gather_columns(y, self.group) if gather and self.world > 1 else y
+        return self.gather(y) if gather else y
+
+    def gather(self, y_local: torch.Tensor) -> torch.Tensor:
+        """NCCL all-gather of this rank's shard outputs, in the unsharded column order."""
+        y = gather_columns(y_local, self.group) if self.world > 1 else y_local
+        return self.in_part_order(y)
+
+    def in_part_order(self, y: torch.Tensor) -> torch.Tensor:
+        return y if self._perm is None else y.index_select(-1, self._perm)

@@ -1,6 +1,7 @@
 """Generate the golden fixtures in tests/golden/ from the REFERENCE's own code.
 
-Run in a container that has the QVex reference tree (default /root/reference):
+Run where the QVex reference tree is on disk ($QVEX_REFERENCE, or a directory named
+``reference`` beside this repository):
 
     python tests/golden/make_golden.py [reference_root]
 

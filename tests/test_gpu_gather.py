@@ -1,14 +1,17 @@
-"""Fused column-sharded decode projection (qvx_qmv_allgather) on two GPUs.
+"""Fused column-sharded decode projection (qvx_qmv_allgather) on all visible GPUs.
 
-Two child processes, one per GPU, set up a PeerGather (CUDA IPC mappings, exchanged over
+One child process per GPU (2, 4 or 8 of them: the largest power of two the box has) sets
+up a PeerGather (CUDA IPC mappings, exchanged over
 a gloo process group: no NCCL) and run sharded projections; each rank's gathered output
 must equal, bit for bit, the single-GPU qvx_qmv of the unsharded weights (a row's
 arithmetic does not depend on how rows are split).  Covered: M = 1, 3 and 8, two calls in
 a row with different inputs, the same projection launched twice back to back (the
 second launch overlaps the first through programmatic dependent launch), one projection
 called with a different token count in between (another grid, so another set of CTAs
-writes each inbox word: the launch tags must still tell old words from new), and slot
-numbers above 120.  Skipped with fewer than two GPUs.
+writes each inbox word: the launch tags must still tell old words from new), slot
+numbers above 120, a fused two-part projection (gathered columns in the unsharded
+[gate | up] order), and PeerGather.reset() between calls.  Skipped with fewer than two
+GPUs.
 """
 import os
 
@@ -40,7 +43,7 @@ def _child(rank, world, port, q):
         qvex.load_library()
         # 120 unused slots first: the projections below use high slot numbers, so a mistake in
         # the per-slot counters or region offsets lands in someone else's memory
-        peer = PeerGather([256] * 120 + [8 * N * 2 for _, _, N in CASES])
+        peer = PeerGather([256] * 120 + [8 * N * 2 for _, _, N in CASES] + [8 * 512 * 2])
         for _ in range(120):
             peer.reserve()
         ok = True
@@ -71,6 +74,22 @@ def _child(rank, world, port, q):
             if not torch.equal(y.view(torch.int16), full(xt).view(torch.int16)):
                 ok = False
                 msgs.append(f"rank {rank} M={M}: back-to-back launches differ")
+        # a fused [gate | up] projection: the gathered columns come back in the unsharded order
+        parts = []
+        for i in range(2):
+            _, _, w, s, b = qmv_inputs(1, 1024, 256, seed=40 + i)
+            parts.append(QLinear(dev(w).view(torch.int32), dev(s).view(torch.bfloat16), dev(b).view(torch.bfloat16)))
+        fused = QLinear.fuse(parts)
+        lin = ShardedQLinear(parts, rank=rank, world=world, peer=peer)
+        xt = dev(qmv_inputs(2, 1024, 8, seed=77)[0]).view(torch.bfloat16)
+        for it in range(2):
+            y = lin(xt).clone()
+            torch.cuda.synchronize()
+            if not torch.equal(y.view(torch.int16), fused(xt).view(torch.int16)):
+                ok = False
+                msgs.append(f"rank {rank}: fused two-part projection differs (call {it})")
+            if it == 0:
+                peer.reset()  # every slot back to zero on every rank; calls carry on from there
         status = qvex._lib.device_status(torch.cuda.current_stream().cuda_stream)
         if status:
             ok = False
@@ -82,14 +101,20 @@ def _child(rank, world, port, q):
         q.put((rank, False, [f"rank {rank}: {type(e).__name__}: {e}"]))
 
 
+def _world():
+    n = min(torch.cuda.device_count(), 8)
+    return 8 if n >= 8 else 4 if n >= 4 else 2 if n >= 2 else 1
+
+
 def test_fused_allgather_matches_single_gpu_qmv():
-    if torch.cuda.device_count() < 2:
+    world = _world()
+    if world < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29600 + os.getpid() % 200
-    procs = [ctx.Process(target=_child, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_child, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]

@@ -67,6 +67,19 @@ def _worker(rank, world, port, case, q):
             a, b = shard_rows(32, world, rank)
             dl = _dense(loc)
             assert torch.equal(dl[:16], _dense(gate)[a:b]) and torch.equal(dl[16:], _dense(up)[a:b])
+        elif case == "fused_gather":
+            # a gathered fused projection (parts of different sizes, as DeltaNet's
+            # qkv|z|b|a) must come back in the column order of the unsharded fuse
+            from qvex.model import QLinear
+            from qvex.shard import ShardedQLinear
+            parts = [_make_linear(n, 64, 10 + i) for i, n in enumerate((32, 16, 8))]
+            fused = QLinear.fuse(parts)
+            sl = ShardedQLinear(parts, rank=rank, world=world)
+            x = torch.from_numpy(np.random.default_rng(5).standard_normal((3, 64)).astype(np.float32))
+            y_loc = x @ _dense(sl.local).T
+            y = sl.gather(y_loc)
+            assert y.shape == (3, 56)
+            assert torch.allclose(y, x @ _dense(fused).T, atol=1e-4)
         elif case == "rank_dies":
             if rank == 1:
                 raise SystemExit(0)  # leaves between steps without joining the collective
@@ -105,7 +118,7 @@ def _run(case, world=2, expect=None):
     return results
 
 
-@pytest.mark.parametrize("case", ["gather", "fused"])
+@pytest.mark.parametrize("case", ["gather", "fused", "fused_gather"])
 def test_sharding_world2(case):
     res = _run(case)
     assert res == {0: "ok", 1: "ok"}, res
@@ -131,9 +144,10 @@ def test_plan_gather_layout():
     outs, inboxes, total = plan_gather_layout([2 * 1024, 300, 16])
     assert outs[0] == 0
     assert all(o % 256 == 0 for o in outs + inboxes)
-    # each slot: its output, then an inbox twice its size
-    assert inboxes[0] == 2048 and outs[1] == inboxes[0] + 4096
-    assert inboxes[1] == outs[1] + 512 and outs[2] == inboxes[1] + 768
+    # each slot: its output, then an inbox four times its size (two halves of one 64-bit
+    # word per output pair)
+    assert inboxes[0] == 2048 and outs[1] == inboxes[0] + 8192
+    assert inboxes[1] == outs[1] + 512 and outs[2] == inboxes[1] + 1280
     assert inboxes[2] == outs[2] + 256 and total == inboxes[2] + 256
     with pytest.raises(ValueError):
         plan_gather_layout([0])
@@ -152,7 +166,7 @@ def test_gather_descriptor_addresses():
         assert d.epoch == 12345 << 8 and d.slot == slot and d.world == 2 and d.rank == 1
         # a slot's inbox lies between its output and the next slot's output
         nxt = outs[slot + 1] if slot + 1 < 150 else total
-        assert outs[slot] + 2 * 4096 <= inboxes[slot] and inboxes[slot] + 4 * 4096 <= nxt
+        assert outs[slot] + 2 * 4096 <= inboxes[slot] and inboxes[slot] + 4 * 2 * 4096 <= nxt
 
 
 
@@ -181,3 +195,14 @@ def test_sharded_qlinear_rejects_odd_rows_for_fused_gather():
     ok = ShardedQLinear(QLinear(torch.zeros(8, 8, dtype=torch.int32), torch.zeros(8, 1, dtype=torch.bfloat16),
                                 torch.zeros(8, 1, dtype=torch.bfloat16)), rank=1, world=2, peer=Peer())
     assert ok.local.w.shape[0] == 4 and Peer.taken == 1
+
+
+def test_part_order_permutation():
+    """Rank-major gathered columns of a fused [a|b] projection map back to [a|b]."""
+    from qvex.shard import part_order
+    sizes, world = [8, 4], 2
+    # gathered: rank 0 holds a[0:4], b[0:2]; rank 1 holds a[4:8], b[2:4]
+    gathered = ["a0", "a1", "a2", "a3", "b0", "b1", "a4", "a5", "a6", "a7", "b2", "b3"]
+    perm = part_order(sizes, world).tolist()
+    assert [gathered[i] for i in perm] == [f"a{i}" for i in range(8)] + [f"b{i}" for i in range(4)]
+    assert sorted(perm) == list(range(12))
