@@ -202,6 +202,76 @@ int qvx_gated_delta(const void* q, const void* k, const void* v, const void* a, 
                     float* state_out, float* state_mid, int B, int T, int Hk, int Hv, int Dk,
                     int Dv, void* stream);
 
+/* ---------------------------------------------------------------- decoder-layer glue */
+
+/* Rounding shared by the normalisations below: a row's sum of squares is reduced as each
+ * thread's 32 consecutive elements in order (FMA), an xor butterfly over a warp's threads
+ * (16, 8, 4, 2, 1), then the warps' totals in order; r = 1/sqrt(sum/D + eps) in IEEE fp32;
+ * out = bf16(w * bf16(x * r)).  The CPU oracle restates exactly this. */
+
+/* mx.fast.rms_norm(x, w, eps) over rows of D (engine/model.py:314,316,335).  With resid
+ * non-NULL the row is first h = bf16(x + resid), the residual add of Layer.__call__
+ * (engine/model.py:315-316), written to h_out when h_out is non-NULL.  w NULL means no
+ * weight.  x, resid, w, h_out, out bf16, 16-byte aligned; D a multiple of 32, <= 32768;
+ * out may alias x, h_out may alias x or resid. */
+int qvx_rms_norm(const void* x, const void* resid, const void* w, float eps, void* h_out, void* out,
+                 long long M, int D, void* stream);
+
+/* out = bf16(a + b) over n bf16 values (n a multiple of 8): the residual add h + mlp(h) of
+ * Layer.__call__ (engine/model.py:316).  out may alias a or b. */
+int qvx_add(const void* a, const void* b, void* out, long long n, void* stream);
+
+/* _gated_rmsnorm (engine/model.py:138-143) for T tokens of H heads of D (D = 32, 64, 128,
+ * 256 or 512): n = rms_norm(y_head, w, eps); out = bf16(z * sigmoid(z) * n) in fp32.
+ * y, out bf16 [T, H*D]; z row t at z + t*z_stride (H*D values, e.g. the z columns of the
+ * in_proj output); w bf16 [D]. */
+int qvx_gated_rms_norm(const void* y, const void* z, long long z_stride, const void* w, float eps,
+                       void* out, long long T, int H, int D, void* stream);
+
+/* _swiglu (engine/model.py:133-135): out[m, i] = bf16(g * sigmoid(g) * u) with row m of gu
+ * at gu + m*gu_stride holding [gate (I) | up (I)] (the fused gate_up output,
+ * engine/model.py:296,301-302).  I and gu_stride multiples of 8. */
+int qvx_swiglu(const void* gu, long long gu_stride, void* out, long long M, long long I, void* stream);
+
+/* GatedDeltaNet.__call__ from the in_proj output to the recurrence inputs
+ * (engine/model.py:259-277): split qkv|z|b|a, depthwise causal conv1d over [conv state;
+ * qkv] with conv_w fp32 [C, conv_kernel] (C = 2*Hk*Dk + Hv*Dv), SiLU, q/k split and
+ * conditioning (q = bf16(1/Dk) * rms_norm(q), k = bf16(1/sqrt(Dk)) * rms_norm(k), eps 1e-6,
+ * per head), and the conv state update.
+ *   proj      bf16 [B, T, proj_stride]: qkv (C) | z (Hv*Dv) | b (Hv) | a (Hv) per row
+ *   state_in  bf16 [B, conv_kernel-1, C]       state_out: the last conv_kernel-1 rows of
+ *   [state_in; qkv]; state_mid (or NULL): the rows before the last token (rollback, :266-267)
+ *   q, k      bf16 [B, T, Hk, Dk]   v bf16 [B, T, Hv, Dv]   a, b bf16 [B, T, Hv]
+ * Dk = Dv in {32, 64, 128, 256}; conv_kernel = 4.  state_out may alias state_in when
+ * T <= 64. */
+int qvx_deltanet_conv(const void* proj, long long proj_stride, const float* conv_w, int conv_kernel,
+                      const void* state_in, void* state_out, void* state_mid, void* q, void* k, void* v,
+                      void* a, void* b, int B, int T, int Hk, int Hv, int Dk, int Dv, void* stream);
+
+/* Bytes of workspace qvx_attention's decode form needs (G = H / Hkv query heads per KV head,
+ * G * L <= 8), or 0 when G * L > 8 (then the prefill form runs and needs none).  The
+ * workspace must be zeroed once before its first use; the kernels leave it reusable. */
+size_t qvx_attention_workspace_size(int B, int Hkv, int G, int L, int D, int nsplit);
+
+/* Attention.__call__ between its projections (engine/model.py:213-232) with
+ * KVCache.update (:156-170), for B sequences of L new tokens at positions
+ * [pos, pos + L) of each:
+ *   qkv       bf16 [B, L, qkv_stride]: H heads of (q (D) | gate (D)), then Hkv keys, then
+ *             Hkv values (q_proj | k_proj | v_proj fused)
+ *   q_norm, k_norm bf16 [D]; inv_freq fp32 [rotary_dim / 2] (base^(-2i/rotary_dim))
+ *   k_cache, v_cache bf16 [B, Hkv, cap, D]: [0, pos) read, [pos, pos + L) written
+ *   q_buf     bf16 [B, L, H, D] scratch (the normalised, rotated queries)
+ *   out       bf16 [B, L, H*D] = sdpa(q, k, v, scale, causal) * sigmoid(gate)
+ * The position is *pos_dev when pos_dev is non-NULL (a device int32, so that one CUDA graph
+ * serves every step), else pos.  With a workspace of qvx_attention_workspace_size(...)
+ * bytes (256-byte aligned) and G * L <= 8 the keys are split over nsplit CTAs per KV head
+ * (decode); otherwise one warp serves eight queries of a head (prefill).  D in {64, 128,
+ * 256}; rotary_dim a multiple of 2*D/32, <= D. */
+int qvx_attention(const void* qkv, long long qkv_stride, const void* q_norm, const void* k_norm, float eps,
+                  const float* inv_freq, int rotary_dim, void* k_cache, void* v_cache, int cap,
+                  const int* pos_dev, int pos, void* q_buf, void* out, int B, int L, int H, int Hkv, int D,
+                  float scale, void* workspace, size_t workspace_bytes, int nsplit, void* stream);
+
 /* ---------------------------------------------------------------- sampling */
 
 /* Replaces Sampler.scores (engine/sampler.py:30-62) for M rows of V logits (bf16 when

@@ -24,8 +24,8 @@ _lib = None
 
 def build(force: bool = False) -> Path:
     """Compile liboracle.so with the committed Makefile (gcc, OpenMP)."""
-    src = HERE / "qvex_oracle.c"
-    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+    srcs = [HERE / "qvex_oracle.c", HERE / "model_oracle.c", HERE / "Makefile"]
+    if force or not LIB_PATH.exists() or any(LIB_PATH.stat().st_mtime < s.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
     return LIB_PATH
 
@@ -50,6 +50,12 @@ def lib():
         L.orc_qk_condition.argtypes = [P, P, I64, I]
         L.orc_sample_scores.argtypes = [P, P, P, I64, I64, ctypes.c_float, ctypes.c_float, I, ctypes.c_float]
         L.orc_sample_scores.restype = I
+        F = ctypes.c_float
+        L.orc_rms_norm.argtypes = [P, P, P, F, P, P, I64, I, I]
+        L.orc_gated_rms_norm.argtypes = [P, P, I64, P, F, P, I64, I, I]
+        L.orc_swiglu.argtypes = [P, I64, P, I64, I64]
+        L.orc_deltanet_conv.argtypes = [P, I64, P, P, P, P, P, P, P, P, P] + [I] * 7
+        L.orc_attention.argtypes = [P, I64, P, P, F, P, I, P, P, I, I, P, I, I, I, I, I, F]
         L.orc_f32_to_bf16.argtypes = [P, P, I64]
         L.orc_bf16_to_f32.argtypes = [P, P, I64]
         L.orc_num_threads.restype = I
@@ -220,3 +226,83 @@ def threads_env() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ layer glue (model_oracle.c)
+
+def rms_norm(x, w=None, eps: float = 1e-6, resid=None, chunk: int = 32):
+    """mx.fast.rms_norm over the last axis (engine/model.py:314,316,335); with ``resid`` the
+    residual add h = x + resid comes first.  Returns out (and h when resid is given)."""
+    x = _u16(x)
+    D = x.shape[-1]
+    M = x.size // D
+    out = np.empty(x.shape, np.uint16)
+    h = np.empty(x.shape, np.uint16) if resid is not None else None
+    r = _u16(resid) if resid is not None else None
+    wv = _u16(w) if w is not None else None
+    lib().orc_rms_norm(_p(x), _p(r) if r is not None else None, _p(wv) if wv is not None else None, eps,
+                       _p(h) if h is not None else None, _p(out), M, D, chunk)
+    return (out, h) if resid is not None else out
+
+
+def gated_rms_norm(y, z, w, eps: float = 1e-6):
+    """_gated_rmsnorm (engine/model.py:138-143): y [T, H, D], z [T, >= H*D] (row stride of
+    its last axis), w [D] -> bf16 [T, H*D]."""
+    y = _u16(y)
+    T, H, D = y.shape
+    z = _u16(z).reshape(T, -1)
+    out = np.empty((T, H * D), np.uint16)
+    lib().orc_gated_rms_norm(_p(y), _p(z), z.shape[1], _p(_u16(w)), eps, _p(out), T, H, D)
+    return out
+
+
+def swiglu(gu):
+    """_swiglu (engine/model.py:133-135) on gu [M, 2I] = [gate | up] -> bf16 [M, I]."""
+    gu = _u16(gu)
+    M, I2 = gu.shape
+    out = np.empty((M, I2 // 2), np.uint16)
+    lib().orc_swiglu(_p(gu), I2, _p(out), M, I2 // 2)
+    return out
+
+
+def deltanet_conv(proj, conv_w, state, Hk, Hv, Dk, Dv, keep_mid: bool = False):
+    """engine/model.py:259-277 up to the gated_delta call.  proj [B, T, >= C + Hv*Dv + 2Hv]
+    (the in_proj output), conv_w fp32 [C, KW], state bf16 [B, KW-1, C].  Returns
+    (q, k, v, a, b, state_out[, state_mid])."""
+    proj = _u16(proj)
+    B, T, S = proj.shape
+    conv_w = np.ascontiguousarray(conv_w, dtype=np.float32)
+    C, KW = conv_w.shape
+    st = _u16(state)
+    q = np.empty((B, T, Hk, Dk), np.uint16)
+    k = np.empty_like(q)
+    v = np.empty((B, T, Hv, Dv), np.uint16)
+    a = np.empty((B, T, Hv), np.uint16)
+    b = np.empty_like(a)
+    so = np.empty((B, KW - 1, C), np.uint16)
+    sm = np.empty_like(so) if keep_mid else None
+    lib().orc_deltanet_conv(_p(proj), S, _p(conv_w), _p(st), _p(so), _p(sm) if keep_mid else None, _p(q), _p(k),
+                            _p(v), _p(a), _p(b), B, T, Hk, Hv, Dk, Dv, KW)
+    return (q, k, v, a, b, so, sm) if keep_mid else (q, k, v, a, b, so)
+
+
+def rope_inv_freq(rd: int, base: float) -> np.ndarray:
+    """fp32 rope frequencies base^(-2i/rd), i < rd/2, computed in double and rounded once."""
+    i = np.arange(rd // 2, dtype=np.float64)
+    return (base ** (-2.0 * i / rd)).astype(np.float32)
+
+
+def attention(qkv, qn, kn, k_cache, v_cache, pos0: int, H: int, Hkv: int, D: int, rd: int, base: float,
+              eps: float = 1e-6, scale: float | None = None):
+    """Attention between its projections (engine/model.py:213-232).  qkv [B, L, H*2D +
+    2*Hkv*D], caches bf16 [B, Hkv, cap, D] (updated in place at [pos0, pos0 + L)).
+    Returns bf16 [B, L, H*D] (the o_proj input)."""
+    qkv = _u16(qkv)
+    B, L, S = qkv.shape
+    cap = k_cache.shape[2]
+    assert k_cache.dtype == np.uint16 and k_cache.flags.c_contiguous and v_cache.flags.c_contiguous
+    out = np.empty((B, L, H * D), np.uint16)
+    inv = rope_inv_freq(rd, base)
+    lib().orc_attention(_p(qkv), S, _p(_u16(qn)), _p(_u16(kn)), eps, _p(inv), rd, _p(k_cache), _p(v_cache), cap,
+                        pos0, _p(out), B, L, H, Hkv, D, D ** -0.5 if scale is None else scale)
+    return out

@@ -40,6 +40,14 @@ SIGNATURES = {
     "qvx_dequantize_rows": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "qvx_gated_delta": (_I, [_P] * 11 + [_I] * 6 + [_P]),
     "qvx_qk_condition": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, _P]),
+    "qvx_rms_norm": (_I, [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_longlong, _I, _P]),
+    "qvx_add": (_I, [_P, _P, _P, ctypes.c_longlong, _P]),
+    "qvx_gated_rms_norm": (_I, [_P, _P, ctypes.c_longlong, _P, ctypes.c_float, _P, ctypes.c_longlong, _I, _I, _P]),
+    "qvx_swiglu": (_I, [_P, ctypes.c_longlong, _P, ctypes.c_longlong, ctypes.c_longlong, _P]),
+    "qvx_deltanet_conv": (_I, [_P, ctypes.c_longlong, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P] + [_I] * 6 + [_P]),
+    "qvx_attention_workspace_size": (_SZ, [_I] * 6),
+    "qvx_attention": (_I, [_P, ctypes.c_longlong, _P, _P, ctypes.c_float, _P, _I, _P, _P, _I, _P, _I, _P, _P]
+                      + [_I] * 5 + [ctypes.c_float, _P, _SZ, _I, _P]),
     "qvx_sample_scores": (_I, [_P, _I, _P, _P, _I, _I, ctypes.c_float, ctypes.c_float, _I, ctypes.c_float, _P]),
     "qvx_sample_pick": (_I, [_P, _P, _I, _I, _I, ctypes.c_ulonglong, ctypes.c_ulonglong, _P]),
 }
