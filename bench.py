@@ -55,6 +55,8 @@ def parse_args():
                     help="N>1: all-gather fused into the qmv kernel (peer stores over NVLink) or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the M=2/4/8 side measurements")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the model-level decode (random-init 9B-shaped model, batch 1 and batch 64)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the config-2/3 kernel measurements (prefill qmm, quantize, gated DeltaNet)")
     ap.add_argument("--profile", nargs="?", const="step", default=None,
@@ -189,6 +191,57 @@ def measure_configs(torch, device, hbm_peak, tc_peak):
         out[f"gated_delta_B{B}_T{T}"] = {"ms": round(ms, 4), "steps_per_s": round(T / ms * 1e3, 1),
                                         "gbs": round((state_bytes + io_bytes) / ms / 1e6, 1),
                                         "fp32_tflops": round(flops / ms / 1e9, 3)}
+    return out
+
+
+def measure_model(torch, device, peak_gbs, decode_steps=256, prefill=4096, batch=64, batch_prefill=128):
+    """Model-level decode of a random-initialised Qwen3.5-9B-shaped 4-bit model (config 4):
+    batch 1 after a `prefill`-token prompt (fed in 512-token chunks, as the reference's engine
+    does), and `batch` sequences after `batch_prefill`-token prompts; greedy decode replayed
+    from one CUDA graph per step (tokens and position stay on the device).  Device-timed
+    with CUDA events; the weights (5 GB with the embedding) exceed L2."""
+    from qvex.qwen35 import Config, DecodeGraph, Qwen35
+    from qvex.sampler import sample_pick, sample_scores
+    from qvex.shapes import Qwen35Shape, qlinear_bytes
+    cfg = Config.qwen35_9b()
+    model = Qwen35.random(cfg, seed=0, device=device)
+    weight_bytes = sum(qlinear_bytes(N, K) for _, N, K in Qwen35Shape().decode_linears())
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    out = {}
+    for B, P in ((1, prefill), (batch, batch_prefill)):
+        cache = model.make_cache(capacity=P + decode_steps + 8)
+        ids = torch.randint(0, cfg.vocab_size, (B, P), device=device, generator=g, dtype=torch.int64).to(torch.int32)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for c0 in range(0, P, 512):
+            logits = model(ids[:, c0:c0 + 512].contiguous(), cache, last_only=True)
+        e1.record()
+        torch.cuda.synchronize()
+        prefill_ms = e0.elapsed_time(e1)
+        first = sample_pick(sample_scores(logits.view(B, -1), temperature=0.0), True).view(B, 1)
+        dg = DecodeGraph(model, cache, first, pos=P)
+        n_warm = 3
+        for _ in range(n_warm):
+            dg.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        steps = decode_steps - n_warm
+        for _ in range(steps):
+            dg.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        key = "batch1" if B == 1 else f"batch{B}"
+        out[key] = {"tok_per_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4), "context": P,
+                    "decode_steps": steps, "prefill_ms": round(prefill_ms, 1),
+                    "prefill_tok_per_s": round(B * P / prefill_ms * 1e3, 1),
+                    "weight_gbs": round(weight_bytes / ms / 1e6, 1),
+                    "frac_hbm_weights": round(weight_bytes / ms / 1e6 / peak_gbs, 3)}
+        del dg, cache
+    del model
+    torch.cuda.empty_cache()
     return out
 
 
@@ -550,6 +603,9 @@ def run_ours(args):
     configs = None
     if world == 1 and not args.no_configs:
         configs = measure_configs(torch, device, peak, tc_peak())
+    model_dec = None
+    if world == 1 and not args.no_model:
+        model_dec = measure_model(torch, device, peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -585,6 +641,8 @@ def run_ours(args):
             rec.update(check)
         if configs:
             rec["configs"] = configs
+        if model_dec:
+            rec["model_decode"] = model_dec
         if cpu:
             rec["cpu_baseline"] = cpu
         print(json.dumps(rec))

@@ -45,7 +45,8 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&v)
 
 __device__ __forceinline__ float rbf16(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
 
-// One CTA per row, one thread per 32 consecutive elements (D / 32 threads, D % 32 == 0).
+// One CTA per row, one thread per 32 consecutive elements (D / 32 of them, D % 32 == 0), the
+// block rounded up to whole warps (threads past the row add zeros to the sums).
 // x, resid, h_out and out may alias (each thread reads its elements before it writes them).
 __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* resid,
                                                         const __nv_bfloat16* __restrict__ w, float eps,
@@ -53,9 +54,15 @@ __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16* x, 
   __shared__ float warp_sum[32];
   const size_t row = blockIdx.x;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+  const bool live = 32 * t < D;
   float v[32];
-  load_bf16x32(x + row * D + 32 * t, v);
-  if (resid) {
+  if (live) {
+    load_bf16x32(x + row * D + 32 * t, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+  }
+  if (resid && live) {
     float r[32];
     load_bf16x32(resid + row * D + 32 * t, r);
 #pragma unroll
@@ -72,6 +79,7 @@ __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16* x, 
   float tot = warp_sum[0];
   for (int i = 1; i < nw; ++i) tot += warp_sum[i];
   const float r = 1.0f / sqrtf(tot / (float)D + eps);
+  if (!live) return;
   if (w) {
     float wv[32];
     load_bf16x32(w + 32 * t, wv);
@@ -181,7 +189,7 @@ extern "C" int qvx_rms_norm(const void* x, const void* resid, const void* w, flo
       (h_out && !aligned(h_out, 16)))
     return fail(QVX_ERR_ALIGN, "qvx_rms_norm: tensors need 16-byte alignment");
   if (M == 0) return QVX_OK;
-  rms_norm_kernel<<<(unsigned)M, D / 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  rms_norm_kernel<<<(unsigned)M, (D / 32 + 31) / 32 * 32, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(resid),
       static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(h_out), static_cast<__nv_bfloat16*>(out),
       D);

@@ -215,24 +215,30 @@ class GatedDeltaNet:
         self.norm_w = p["norm"]
         self.out_proj = _qlin(p["out_proj"])
 
-    def mix(self, x: torch.Tensor, cache: RecurrentCache, keep_prev: bool = False) -> torch.Tensor:
-        """The out_proj input [B, S, Hv*Dv] (everything of __call__ but out_proj)."""
+    def init_state(self, cache: RecurrentCache, B: int, device) -> None:
+        """Zero conv window and recurrent state for B sequences."""
+        cache.conv = torch.zeros((B, self.K - 1, self.conv_dim), dtype=torch.bfloat16, device=device)
+        cache.ssm = torch.zeros((B, self.hv, self.dv, self.dk), dtype=torch.float32, device=device)
+
+    def mix(self, x: torch.Tensor, cache: RecurrentCache, keep_prev: bool = False,
+            inplace: bool = False) -> torch.Tensor:
+        """The out_proj input [B, S, Hv*Dv] (everything of __call__ but out_proj).  With
+        ``inplace`` the conv window and recurrent state are updated in their own buffers (the
+        form a CUDA graph replays); otherwise new tensors replace them, as in the reference."""
         B, S, _ = x.shape
         proj = self.in_proj(x)
-        conv_state = cache.conv
-        if conv_state is None:
-            conv_state = torch.zeros((B, self.K - 1, self.conv_dim), dtype=torch.bfloat16, device=x.device)
-        r = glue.deltanet_conv(proj, self.conv_w, conv_state, self.hk, self.hv, self.dk, self.dv, keep_mid=keep_prev)
+        if cache.conv is None:
+            self.init_state(cache, B, x.device)
+        r = glue.deltanet_conv(proj, self.conv_w, cache.conv, self.hk, self.hv, self.dk, self.dv, keep_mid=keep_prev,
+                               state_out=cache.conv if inplace else None)
         q, k, v, a, b, cache.conv = r[:6]
         if keep_prev:
             cache.conv_prev = r[6]
-        state = cache.ssm
-        if state is None:
-            state = torch.zeros((B, self.hv, self.dv, self.dk), dtype=torch.float32, device=x.device)
+        g = gated_delta(q, k, v, a, b, self.A_log, self.dt_bias, cache.ssm, keep_mid=keep_prev,
+                        out_state=cache.ssm if inplace else None)
+        y, cache.ssm = g[0], g[1]
         if keep_prev:
-            y, cache.ssm, cache.ssm_prev = gated_delta(q, k, v, a, b, self.A_log, self.dt_bias, state, keep_mid=True)
-        else:
-            y, cache.ssm = gated_delta(q, k, v, a, b, self.A_log, self.dt_bias, state)
+            cache.ssm_prev = g[2]
         cache.offset += S
         z = proj.view(B * S, -1)[:, self.conv_dim:self.conv_dim + self.value_dim]
         return glue.gated_rms_norm(y, z, self.norm_w, self.cfg.rms_norm_eps).view(B, S, self.value_dim)
@@ -263,18 +269,23 @@ class Layer:
         self.ln1, self.ln2 = p["input_layernorm"], p["post_attention_layernorm"]
         self.eps = cfg.rms_norm_eps
 
-    def _mixer(self, n, cache, keep_prev):
-        return self.mixer(n, cache, keep_prev) if self.linear else self.mixer(n, cache)
+    def _mixer(self, n, cache, keep_prev, pos=None):
+        if self.linear:
+            return self.mixer.out_proj(self.mixer.mix(n, cache, keep_prev, inplace=pos is not None))
+        return self.mixer.o_proj(self.mixer.mix(n, cache, pos))
 
-    def forward_deferred(self, x: torch.Tensor, pending: torch.Tensor | None, cache, keep_prev: bool = False):
+    def forward_deferred(self, x: torch.Tensor, pending: torch.Tensor | None, cache, keep_prev: bool = False,
+                         pos=None):
         """The layer on the residual stream x + pending (pending None: x alone), with this
         layer's MLP output returned unadded: (h, mlp_out) such that the layer's output is
-        h + mlp_out.  The add then rides in the next rms_norm (one kernel less per layer)."""
+        h + mlp_out.  The add then rides in the next rms_norm (one kernel less per layer).
+        ``pos`` (device int32) selects the graph-replayable form: states updated in place,
+        attention positions read on the device."""
         if pending is None:
             n = glue.rms_norm(x, self.ln1, self.eps)
         else:
             n, x = glue.rms_norm(pending, self.ln1, self.eps, resid=x)
-        m = self._mixer(n, cache, keep_prev)
+        m = self._mixer(n, cache, keep_prev, pos)
         n2, h = glue.rms_norm(m, self.ln2, self.eps, resid=x)
         return h, self.mlp(n2)
 
@@ -293,14 +304,34 @@ class Qwen35:
     def make_cache(self, capacity: int | None = None):
         return [RecurrentCache() if l.linear else KVCache(capacity) for l in self.layers]
 
-    def hidden(self, ids: torch.Tensor, cache, keep_prev: bool = False):
+    def hidden(self, ids: torch.Tensor, cache, keep_prev: bool = False, pos=None):
         """(h, pending): the pre-norm hidden state is h + pending (the last MLP output not yet
         added)."""
         x = self.embed(ids)
         pending = None
         for layer, c in zip(self.layers, cache):
-            x, pending = layer.forward_deferred(x, pending, c, keep_prev)
+            x, pending = layer.forward_deferred(x, pending, c, keep_prev, pos)
         return x, pending
+
+    def prepare_decode(self, cache, B: int, device) -> None:
+        """Allocates every state buffer a graph-replayed decode step updates in place: zero
+        recurrent states where none exist yet; KV caches at their fixed capacity."""
+        for layer, c in zip(self.layers, cache):
+            if layer.linear:
+                if c.conv is None:
+                    layer.mixer.init_state(c, B, device)
+            else:
+                if c.capacity is None:
+                    raise ValueError("graph decode needs KV caches of fixed capacity (make_cache(capacity))")
+                c.reserve(B, layer.mixer.n_kv, layer.mixer.head_dim, 0, device)
+
+    def decode_step(self, ids: torch.Tensor, cache, pos: torch.Tensor) -> torch.Tensor:
+        """One decode step of B sequences, ids [B, 1] int32 at the device position ``pos``
+        (int32 [1]): every state updated in its own buffer and nothing read on the host, so the
+        step can be captured once and replayed for every token.  Returns logits [B, 1, V]."""
+        x, pending = self.hidden(ids, cache, pos=pos)
+        n = glue.rms_norm(pending, self.norm, self.cfg.rms_norm_eps, resid=x)[0]
+        return self.lm_head(n)
 
     def __call__(self, ids: torch.Tensor, cache, last_only: bool = True, return_hidden: bool = False,
                  keep_prev: bool = False):
@@ -413,3 +444,69 @@ def random_params(cfg: Config, seed: int, device) -> dict:
             P[f"{sa}.k_norm.weight"] = norm(cfg.head_dim)
     P["model.norm.weight"] = norm(h)
     return P
+
+
+class DecodeGraph:
+    """Greedy decode of B sequences with one CUDA graph per step (the decode loop of
+    engine/speculative.py:103-118 without host round trips): embed the current tokens, run
+    every layer at the device position, final norm, lm_head, argmax; the picked tokens are
+    the next step's input and the position advances on the device.  ``run(n)`` replays the
+    graph n times and returns the n x B tokens.  The caches must come from
+    ``model.make_cache(capacity)``; states before the graph are kept (warm-up is undone)."""
+
+    def __init__(self, model: Qwen35, cache, first_ids: torch.Tensor, pos: int):
+        from .sampler import sample_pick, sample_scores
+        self.model, self.cache = model, cache
+        dev = first_ids.device
+        B = first_ids.shape[0]
+        self.B = B
+        model.prepare_decode(cache, B, dev)
+        self.ids = first_ids.reshape(B, 1).to(torch.int32).clone()
+        self.pos = torch.tensor([pos], dtype=torch.int32, device=dev)
+        self.start = pos
+        self.steps = 0
+        self.hist = None
+
+        def step():
+            logits = model.decode_step(self.ids, cache, self.pos)
+            scores = sample_scores(logits.view(B, -1), temperature=0.0)
+            sample_pick(scores, True, out=self.ids)
+            self.pos.add_(1)
+            return logits
+
+        # warm-up outside the graph (module loads, launch attributes, workspaces), then undo
+        # its state changes so the graph starts from the caller's state
+        saved = [(c.conv.clone(), c.ssm.clone()) if isinstance(c, RecurrentCache) else None for c in cache]
+        ids0 = self.ids.clone()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for c, sv in zip(cache, saved):
+            if sv is not None:
+                c.conv.copy_(sv[0])
+                c.ssm.copy_(sv[1])
+        self.ids.copy_(ids0)
+        self.pos.fill_(pos)
+        offsets = [c.offset for c in cache]
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = step()
+        for c, o in zip(cache, offsets):  # capture ran the Python side once more
+            c.offset = o
+
+    def replay(self) -> None:
+        """One decode step on the current stream (no host synchronisation)."""
+        self.graph.replay()
+        self.steps += 1
+        for c in self.cache:
+            c.offset += 1
+
+    def run(self, n: int) -> torch.Tensor:
+        """n steps; returns the tokens picked at each step, int32 [n, B] (one sync at the end)."""
+        out = torch.empty((n, self.B), dtype=torch.int32, device=self.ids.device)
+        for i in range(n):
+            self.replay()
+            out[i].copy_(self.ids.view(-1))
+        return out

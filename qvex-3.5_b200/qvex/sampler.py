@@ -49,15 +49,22 @@ def sample_scores(logits: torch.Tensor, temperature: float = 0.6, top_p: float =
     return out.reshape(logits.shape)
 
 
-def sample_pick(scores: torch.Tensor, greedy: bool, seed: int = 0, offset: int = 0) -> torch.Tensor:
-    """int32 tokens [...] from fp32 scores [..., V] (Sampler.pick)."""
+def sample_pick(scores: torch.Tensor, greedy: bool, seed: int = 0, offset: int = 0, *,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """int32 tokens [...] from fp32 scores [..., V] (Sampler.pick); ``out`` (contiguous int32,
+    one element per row) receives them when given."""
     _require_cuda("scores", scores, (torch.float32,))
     V = scores.shape[-1]
     s = scores.reshape(-1, V).contiguous()
-    tok = torch.empty(s.shape[0], dtype=torch.int32, device=s.device)
+    if out is not None:
+        if out.dtype != torch.int32 or out.numel() != s.shape[0] or not out.is_contiguous():
+            raise ValueError("out must be a contiguous int32 tensor with one element per row")
+        tok = out.view(-1)
+    else:
+        tok = torch.empty(s.shape[0], dtype=torch.int32, device=s.device)
     check(lib().qvx_sample_pick(_ptr(s), _ptr(tok), s.shape[0], V, 1 if greedy else 0, seed & (2**64 - 1),
                                 offset & (2**64 - 1), _stream(s)), "qvx_sample_pick")
-    return tok.reshape(scores.shape[:-1])
+    return out if out is not None else tok.reshape(scores.shape[:-1])
 
 
 class Sampler:

@@ -100,3 +100,32 @@ def test_layer_call_matches_deferred_residual(models):
     a = layer(x, model.make_cache()[0])
     h, mo = layer.forward_deferred(x, None, model.make_cache()[0])
     assert torch.equal(a.view(torch.int16), glue.add(h, mo).view(torch.int16))
+
+
+def test_graph_decode_matches_eager_greedy(models):
+    """DecodeGraph (one CUDA graph per step, position and tokens on the device, states
+    updated in place) picks the same tokens as eager greedy decoding, bit for bit."""
+    cfg, model, P = models
+    from qvex.qwen35 import DecodeGraph
+    from qvex.sampler import sample_pick, sample_scores
+    rng = np.random.default_rng(2)
+    B, L, n = 2, 12, 6
+    ids = torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, L)).astype(np.int32)).cuda()
+
+    cache = model.make_cache(capacity=64)
+    logits = model(ids, cache, last_only=True)
+    tok = sample_pick(sample_scores(logits.view(B, -1), temperature=0.0), True).view(B, 1)
+    eager = []
+    for _ in range(n):
+        logits = model(tok, cache, last_only=True)
+        tok = sample_pick(sample_scores(logits.view(B, -1), temperature=0.0), True).view(B, 1)
+        eager.append(tok.view(-1).clone())
+    eager = torch.stack(eager)
+
+    cache = model.make_cache(capacity=64)
+    logits = model(ids, cache, last_only=True)
+    first = sample_pick(sample_scores(logits.view(B, -1), temperature=0.0), True).view(B, 1)
+    g = DecodeGraph(model, cache, first, pos=L)
+    got = g.run(n)
+    assert torch.equal(got, eager), (got, eager)
+    assert all(c.offset == L + n for c in cache)

@@ -441,3 +441,65 @@ def test_qmm_workspace_reuse_and_out(qvex):
     for _ in range(2):
         qvex.quantized_matmul(dev(x), dev(w), dev(s), dev(b), out=out, workspace=ws)
     assert rel_l2(host_u16(out), ref) <= MATMUL_TOL
+
+
+# ------------------------------------------------------------------ every shape of the benchmark's decode step
+
+CONFIG1_SHAPES = [(12352, 4096), (4096, 4096), (8192, 4096), (1024, 4096), (10240, 4096), (24576, 4096),
+                  (4096, 12288)]  # in_proj, out/o_proj, q_proj, k/v_proj, fused q|k|v, gate_up, down
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+@pytest.mark.parametrize("N,K", CONFIG1_SHAPES)
+def test_qmv_config1_shapes(qvex, M, N, K):
+    """Every distinct projection shape of the Qwen3.5-9B decode step at the verify widths
+    M = 1, 2, 4, 8 (the streaming kernel's one- and two-token plans, all row tilings)."""
+    x, _, w, s, b = qmv_inputs(M, K, N, seed=7 * M + N + K)
+    y = qvex.quantized_matmul(dev(x), dev(w), dev(s), dev(b))
+    ref = O.qmm_exact(x, w, s, b)
+    torch.cuda.synchronize()
+    assert rel_l2(host_u16(y), ref) <= MATMUL_TOL
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+def test_qmv_lm_head_sampled(qvex, M):
+    """lm_head [248320, 4096] (572 MB, one launch) at M = 1, 2, 4, 8; the oracle checks every
+    97th output row (2560 rows, all M tokens)."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(M)
+    N, K = 248320, 4096
+    w = torch.randint(-2 ** 31, 2 ** 31, (N, K // 8), dtype=torch.int64, device="cuda", generator=g).to(torch.int32)
+    s = (torch.randn((N, K // 64), device="cuda", generator=g).abs() * 0.002).to(torch.bfloat16)
+    b = (-8.0 * s.float()).to(torch.bfloat16)
+    x = torch.randn((M, K), device="cuda", generator=g).to(torch.bfloat16)
+    y = qvex.quantized_matmul(x, w, s, b)
+    rows = slice(None, None, 97)
+    ref = O.qmm_exact(host_u16(x), w[rows].cpu().numpy().view(np.uint32), host_u16(s[rows]), host_u16(b[rows]))
+    torch.cuda.synchronize()
+    assert rel_l2(host_u16(y[:, rows].contiguous()), ref) <= MATMUL_TOL
+
+
+def test_gated_delta_config3_b8_t2048_with_rollback(qvex):
+    """Config 3 at its benchmarked size: B = 8, T = 2048, N(0,1)*0.1 state, A_log = dt_bias = 0;
+    y and the final state against the oracle, and the snapshot before the last step
+    reproduces the final state when the last step is rerun from it (bitwise)."""
+    g = torch.Generator().manual_seed(77)
+    B, T, Hk, Hv, D = 8, 2048, 16, 32, 128
+
+    def bf16(t):
+        return O.f32_to_bf16(t.numpy().astype(np.float32))
+    q = bf16(torch.nn.functional.normalize(torch.randn((B, T, Hk, D), generator=g), dim=-1))
+    k = bf16(torch.nn.functional.normalize(torch.randn((B, T, Hk, D), generator=g), dim=-1))
+    v = bf16(torch.randn((B, T, Hv, D), generator=g))
+    a = bf16(torch.randn((B, T, Hv), generator=g))
+    b = bf16(torch.randn((B, T, Hv), generator=g))
+    st = (torch.randn((B, Hv, D, D), generator=g) * 0.1).numpy()
+    zeros = np.zeros(Hv, np.float32)
+    y, so, sm = run_gd(qvex, q, k, v, a, b, zeros, zeros, st, True)
+    ry, rs = O.gated_delta(q, k, v, a, b, zeros, zeros, st)
+    assert rel_l2(y, ry) <= MATMUL_TOL
+    assert rel_l2(so, rs) <= STATE_TOL
+    # rerun the last step from the snapshot
+    last = [np.ascontiguousarray(t[:, -1:]) for t in (q, k, v, a, b)]
+    y2, so2 = run_gd(qvex, *last, zeros, zeros, sm, False)
+    assert np.array_equal(so2, so) and np.array_equal(y2, y[:, -1:])
