@@ -126,7 +126,11 @@ typedef struct qvx_gather {
   int n_total; /* rows of the whole projection (world * N) */
   int row0;    /* first row of this rank's shard (rank * N) */
   int slot;    /* index into epoch (two words per slot) */
+  int mode;    /* qvx_qmv_fused: QVX_EXCHANGE_GATHER or QVX_EXCHANGE_REDUCE (qvx_qmv_allgather ignores it) */
 } qvx_gather;
+
+#define QVX_EXCHANGE_GATHER 0
+#define QVX_EXCHANGE_REDUCE 1
 
 /* Column-sharded decode projection with its all-gather fused in: y = x @ dequant(w)^T
  * for this rank's N rows, written into out[rank]; each CTA also sends its rows to every
@@ -141,6 +145,64 @@ typedef struct qvx_gather {
 int qvx_qmv_allgather(const void* x, const uint32_t* w, const void* scales, const void* biases,
                       const qvx_gather* g, int M, int N, int K, int group_size, int bits,
                       void* stream);
+
+/* ---------------------------------------------------------------- fused decode projection */
+
+/* What a fused decode projection computes its input from (prologue) and adds to its
+ * output (epilogue).  Each prologue runs on the slice of x every thread already loads, with
+ * the arithmetic and reduction order of the standalone kernel it replaces, so fused and
+ * unfused paths give the same bits:
+ *   QVX_IN_PLAIN            x as given
+ *   QVX_IN_RMS_NORM         rms_norm(x, norm_w [K], eps) over the whole row (qvx_rms_norm):
+ *                           a decoder layer's input norms and the final norm in front of
+ *                           lm_head (engine/model.py:314,316,335)
+ *   QVX_IN_SWIGLU           silu(x[:, :K]) * x[:, K:2K] (qvx_swiglu): the MLP's down input
+ *                           (engine/model.py:302)
+ *   QVX_IN_GATED_RMS_NORM   per head of head_dim: rms_norm(x, norm_w [head_dim], eps) *
+ *                           silu(z) (qvx_gated_rms_norm): DeltaNet's out_proj input
+ *                           (engine/model.py:289-291)
+ * Epilogue: with resid non-NULL, y = bf16(resid + bf16(x @ W^T)), the residual add of
+ * engine/model.py:315-316 (resid bf16 [M, N] row-major, may alias y). */
+enum qvx_qmv_prologue {
+  QVX_IN_PLAIN = 0,
+  QVX_IN_RMS_NORM = 1,
+  QVX_IN_SWIGLU = 2,
+  QVX_IN_GATED_RMS_NORM = 3
+};
+
+typedef struct qvx_qmv_io {
+  int prologue;          /* enum qvx_qmv_prologue */
+  long long x_stride;    /* elements between token rows of x; 0 means K (2K for SWIGLU) */
+  const void* norm_w;    /* RMS_NORM: bf16 [K]; GATED_RMS_NORM: bf16 [head_dim] */
+  const void* z;         /* GATED_RMS_NORM: bf16, token row m at z + m * z_stride */
+  long long z_stride;
+  int head_dim;          /* GATED_RMS_NORM: 32 .. 1024, a power of two dividing K */
+  float eps;
+  const void* resid;     /* epilogue residual or NULL */
+} qvx_qmv_io;
+
+/* The decode projection (M <= 8, K % 512 == 0, K <= 12288) with a prologue and epilogue
+ * (io may be NULL: plain), optionally sharded (g may be NULL: one GPU):
+ *   g == NULL                  y bf16 [M, N] = epilogue(prologue(x) @ dequant(w)^T)
+ *   g->mode == QVX_EXCHANGE_GATHER   column-sharded with the all-gather fused in, as
+ *                              qvx_qmv_allgather (y unused; no residual epilogue)
+ *   g->mode == QVX_EXCHANGE_REDUCE   row-parallel: this rank holds K columns of the weight
+ *                              (its slice of the inputs, e.g. its heads of DeltaNet's
+ *                              out_proj or its slice of the MLP's down projection) and every
+ *                              rank computes partial sums for all N rows; the partials are
+ *                              exchanged between twin CTAs over NVLink as (fp32, tag) words
+ *                              and summed in rank order, so every rank's y holds the same
+ *                              bits.  g->out[rank]: this rank's fp32 [M, N] partial buffer
+ *                              (16-byte aligned); g->inbox[r]: rank r's receive area of
+ *                              2 * world * M * N 64-bit words; n_total = N, row0 = 0; y bf16
+ *                              [M, N] gets the sum (and the residual epilogue).
+ * Replaces, per decode step of the reference (engine/model.py:257-316), the projections
+ * and the glue kernels around them.  The sharded forms follow qvx_qmv_allgather's rules
+ * (every rank makes the same calls; a rank that never arrives makes the others give up
+ * after 2 s with QVX_ERR_TIMEOUT; after a failure, reset as described at qvx_gather). */
+int qvx_qmv_fused(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                  int M, int N, int K, int group_size, int bits, const qvx_qmv_io* io,
+                  const qvx_gather* g, void* stream);
 
 /* Dispatcher with mx.quantized_matmul's semantics: qvx_qmv for M <= 8, qvx_qmm above.
  * The workspace may be NULL when M <= 8. */

@@ -252,8 +252,9 @@ static int launch_qmv(const void* x, const uint32_t* w, const void* s, const voi
 }
 
 struct QmvGather;
+struct QmvIO;
 int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
-                   cudaStream_t stream, const QmvGather* gather = nullptr);
+                   cudaStream_t stream, const QmvGather* gather = nullptr, const QmvIO* io = nullptr);
 
 int qmv_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
                 int M, int N, int K, cudaStream_t stream) {

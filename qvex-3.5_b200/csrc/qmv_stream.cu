@@ -46,6 +46,8 @@ constexpr size_t kStreamSmemBudget = 200 * 1024;
 // Codes per stage: measured on B200, 16 KB stages (4 rows per team at K = 4096) stream
 // lm_head at ~80% of HBM against ~63% for 8 KB stages.
 constexpr size_t kStreamStageCodeBytes = 16384;
+// per-warp row sums of the rms_norm prologue: [2 tokens][compute warps]
+constexpr size_t kStreamRowSsBytes = 2 * 16 * sizeof(float);
 
 template <int NV>
 struct VCfg {
@@ -77,14 +79,48 @@ __device__ __forceinline__ void reduce_transpose(float* p, int lane) {
   }
 }
 
-// Destination of the fused column-sharded form (qvx_qmv_allgather); world == 0 for the
-// plain qvx_qmv form.  A copy of qvx_gather in the kernel's parameter space.
+// Exchange of the sharded forms; world == 0 for the plain form.  A copy of qvx_gather in the
+// kernel's parameter space.  mode kExGather (column-sharded, qvx_qmv_allgather): out[rank]
+// is this rank's full bf16 output.  mode kExReduce (row-parallel, K sharded): out[rank] is
+// this rank's fp32 partial sums [M, N], and the summed result goes to y.
+constexpr int kExGather = 0, kExReduce = 1;
 struct QmvGather {
   __nv_bfloat16* out[QVX_MAX_RANKS];
   unsigned long long* inbox[QVX_MAX_RANKS];
   unsigned* epoch;
-  int world, rank, n_total, row0, slot;
+  int world, rank, n_total, row0, slot, mode;
 };
+
+// What the kernel computes x from (prologue) and what it adds to y (epilogue); a copy of
+// qvx_qmv_io.  Prologues (each lane transforms its own 32 inputs of every token, with the
+// arithmetic and reduction order of the standalone kernels of glue.cu, so that the fused
+// and unfused paths give the same bits):
+//   kInPlain     x as given (row m at x + m * x_stride)
+//   kInRmsNorm   rms_norm(x, norm_w, eps) over the whole row of K (qvx_rms_norm)
+//   kInSwiglu    silu(x[:, :K]) * x[:, K:2K] (qvx_swiglu; x is the gate|up output)
+//   kInGatedRms  x = y per head of 32 * head_lanes, rms_norm(y, norm_w) * silu(z)
+//                (qvx_gated_rms_norm; z row m at z + m * z_stride)
+// Epilogue: with resid, y = bf16(resid + bf16(acc)) (the residual add of a decoder layer).
+constexpr int kInPlain = 0, kInRmsNorm = 1, kInSwiglu = 2, kInGatedRms = 3;
+struct QmvIO {
+  int in_mode;
+  long long x_stride;
+  const __nv_bfloat16* norm_w;
+  const __nv_bfloat16* z;
+  long long z_stride;
+  int head_lanes;
+  float eps;
+  const __nv_bfloat16* resid;
+};
+
+__device__ __forceinline__ float rbf(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+         ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+}
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 // Flag-in-data words: a 64-bit store or load is single-copy atomic, so the tag in the high
 // half proves that the two bf16 values in the low half are from the same launch -- no
@@ -168,8 +204,8 @@ __device__ __forceinline__ void make_planes(const uint32_t (&u)[16], XPlanes<PL>
 template <int MC, int RT, bool FULLK, int S>
 __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     qmv_stream_kernel(const __nv_bfloat16* __restrict__ x, const uint32_t* __restrict__ w,
-                      const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, __nv_bfloat16* __restrict__ y,
-                      int M, int N, int K, int T, int* status, const QmvGather g) {
+                      const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, __nv_bfloat16* y,
+                      int M, int N, int K, int T, int* status, const QmvGather g, const QmvIO io) {
   using VC = VCfg<RT * MC>;
   constexpr int V = VC::V, LV = VC::LV;
   constexpr int PL = MC == 1 ? 3 : 2;  // x planes (see XPlanes)
@@ -186,6 +222,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
   uint64_t* done = full + S;
   uint64_t* empty = done + S;
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(empty + S);
+  float* row_ss = reinterpret_cast<float*>(smem + S * stage_bytes + 3 * S * sizeof(uint64_t) + 16);  // [MC][CW]
 
   const int m0 = blockIdx.y * MC;
   const int mc = min(MC, M - m0);
@@ -244,16 +281,92 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     const bool kact = FULLK || k0 < K;
     const int g = kact ? (k0 >> 6) : 0;
     pdl_wait();  // x comes from the upstream kernel
-    XPlanes<PL> xp[MC];
-#pragma unroll
-    for (int m = 0; m < MC; ++m) {
-      const bool live = kact && m < mc;
-      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(m0 + (live ? m : 0)) * K + (live ? k0 : 0));
-      uint32_t u[16];
+    auto xrow = [&](int m) { return x + (size_t)(m0 + m) * io.x_stride; };
+    // a lane's 32 inputs of token m as 16 packed bf16 pairs (zeros when out of range)
+    auto load_raw = [&](int m, bool live, uint32_t (&u)[16]) {
+      const uint4* src = reinterpret_cast<const uint4*>(xrow(live ? m : 0) + (live ? k0 : 0));
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint4 t = live ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
         u[4 * c] = t.x; u[4 * c + 1] = t.y; u[4 * c + 2] = t.z; u[4 * c + 3] = t.w;
+      }
+    };
+    auto sumsq = [&](const uint32_t (&u)[16]) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+        ss = fmaf(a, a, ss);
+        ss = fmaf(b, b, ss);
+      }
+      return ss;
+    };
+    if (io.in_mode == kInRmsNorm) {
+      // the row's sum of squares: a lane's 32 inputs in order, a butterfly over the warp,
+      // then the warps of the team in order (qvx_rms_norm's order)
+#pragma unroll
+      for (int m = 0; m < MC; ++m) {
+        uint32_t u[16];
+        load_raw(m, kact && m < mc, u);
+        float ss = sumsq(u);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) row_ss[m * CW + warp] = ss;
+      }
+      named_barrier(1, CW * 32);
+    }
+    XPlanes<PL> xp[MC];
+#pragma unroll
+    for (int m = 0; m < MC; ++m) {
+      const bool live = kact && m < mc;
+      uint32_t u[16];
+      load_raw(m, live, u);
+      if (io.in_mode != kInPlain) {
+        // the transform in chunks of 8 inputs (one 16-byte piece of every operand at a time)
+        float r = 0.0f;
+        if (io.in_mode == kInRmsNorm) {
+          float tot = row_ss[m * CW + team * P];
+          for (int p = 1; p < P; ++p) tot += row_ss[m * CW + team * P + p];
+          r = 1.0f / sqrtf(tot / (float)K + io.eps);
+        } else if (io.in_mode == kInGatedRms) {
+          float ss = sumsq(u);
+          for (int o = io.head_lanes / 2; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          r = 1.0f / sqrtf(ss / (float)(32 * io.head_lanes) + io.eps);
+        }
+        if (live) {
+          const uint4* aux = io.in_mode == kInRmsNorm ? reinterpret_cast<const uint4*>(io.norm_w + k0)
+                             : io.in_mode == kInSwiglu ? reinterpret_cast<const uint4*>(xrow(m) + K + k0)
+                                                       : reinterpret_cast<const uint4*>(io.z + (size_t)(m0 + m) * io.z_stride + k0);
+          const uint4* wn = reinterpret_cast<const uint4*>(io.norm_w + (lane % max(io.head_lanes, 1)) * 32);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 a4 = __ldg(aux + c);
+            const uint32_t av[4] = {a4.x, a4.y, a4.z, a4.w};
+            uint4 w4 = make_uint4(0, 0, 0, 0);
+            if (io.in_mode == kInGatedRms) w4 = __ldg(wn + c);
+            const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float v2[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t xs = h ? (u[4 * c + j] & 0xffff0000u) : (u[4 * c + j] << 16);
+                const uint32_t as = h ? (av[j] & 0xffff0000u) : (av[j] << 16);
+                const float xv = __uint_as_float(xs), aa = __uint_as_float(as);
+                if (io.in_mode == kInRmsNorm) {
+                  v2[h] = aa * rbf(xv * r);
+                } else if (io.in_mode == kInSwiglu) {
+                  v2[h] = xv * (1.0f / (1.0f + expf(-xv))) * aa;
+                } else {
+                  const float ww = __uint_as_float(h ? (wv[j] & 0xffff0000u) : (wv[j] << 16));
+                  const float nrm = rbf(ww * rbf(xv * r));
+                  v2[h] = aa * (1.0f / (1.0f + expf(-aa))) * nrm;
+                }
+              }
+              u[4 * c + j] = bf16x2_bits(v2[0], v2[1]);
+            }
+          }
+        }
       }
       make_planes<PL>(u, xp[m]);
     }
@@ -330,6 +443,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     }
   } else {
     // ------------------------------------------------------------ reducer
+    if (io.resid) pdl_wait();  // the residual comes from the upstream kernel
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % S;
       const uint32_t ph = (uint32_t)(c / S) & 1u;
@@ -343,13 +457,20 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
         if (r < nr && m < mc) {
           float acc = 0.0f;
           for (int p = 0; p < P; ++p) acc += red[(team * P + p) * 32 + idx];
-          const __nv_bfloat16 yv = __float2bfloat16_rn(acc);
-          if (gather) {
-            // this rank's own full output; the peers get the CTA's rows once, at the end
-            // (a peer store here would make every stage release wait for NVLink)
-            g.out[g.rank][(size_t)(m0 + m) * g.n_total + g.row0 + r0 + r] = yv;
+          if (gather && g.mode == kExReduce) {
+            // this rank's partial sums over its K slice; summed over the ranks at the end
+            reinterpret_cast<float*>(g.out[g.rank])[(size_t)(m0 + m) * N + r0 + r] = acc;
           } else {
-            y[(size_t)(m0 + m) * N + r0 + r] = yv;
+            __nv_bfloat16 yv = __float2bfloat16_rn(acc);
+            if (io.resid)
+              yv = __float2bfloat16_rn(__bfloat162float(io.resid[(size_t)(m0 + m) * N + r0 + r]) + __bfloat162float(yv));
+            if (gather) {
+              // this rank's own full output; the peers get the CTA's rows once, at the end
+              // (a peer store here would make every stage release wait for NVLink)
+              g.out[g.rank][(size_t)(m0 + m) * g.n_total + g.row0 + r0 + r] = yv;
+            } else {
+              y[(size_t)(m0 + m) * N + r0 + r] = yv;
+            }
           }
         }
       }
@@ -376,9 +497,52 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       pdl_wait();
       __syncwarp();
       const unsigned tag = *reinterpret_cast<volatile unsigned*>(g.epoch + 2 * g.slot) + 1u;
+      const size_t half = (size_t)(tag & 1u);
+      if (g.mode == kExReduce) {
+        // Row-parallel all-reduce by the same flag-in-data words: the twin CTAs cover the
+        // same output rows [r_begin, r_end) of every rank's partial sums.  Each CTA sends its
+        // partials (fp32, tag) to every peer's inbox at [half][this rank][token][row], then
+        // sums the ranks' partials of its rows in rank order -- the same bits on every rank --
+        // rounds to bf16 and applies the residual epilogue.
+        const float* part = reinterpret_cast<const float*>(g.out[g.rank]);
+        for (int m = 0; m < mc; ++m)
+          for (int j = r_begin + lane; j < r_end; j += 32) {
+            const size_t e = (size_t)(m0 + m) * N + j;
+            const unsigned long long word = (unsigned long long)__float_as_uint(part[e]) | ((unsigned long long)tag << 32);
+            for (int q = 0; q < g.world; ++q)
+              if (q != g.rank) st_relaxed_sys_u64(g.inbox[q] + (half * g.world + g.rank) * (size_t)M * N + e, word);
+          }
+        const unsigned long long t0 = globaltimer_ns();
+        bool late = false;
+        for (int m = 0; m < mc && !late; ++m)
+          for (int j = r_begin + lane; j < r_end && !late; j += 32) {
+            const size_t e = (size_t)(m0 + m) * N + j;
+            float tot = 0.0f;
+            for (int q = 0; q < g.world && !late; ++q) {
+              float v = part[e];
+              if (q != g.rank) {
+                const unsigned long long* src = g.inbox[g.rank] + (half * g.world + q) * (size_t)M * N + e;
+                unsigned long long word = ld_relaxed_sys_u64(src);
+                for (uint32_t it = 1; (unsigned)(word >> 32) != tag; ++it) {
+                  if ((it & 63) == 0 && (globaltimer_ns() - t0 > kWaitTimeoutNs || it > kWaitMaxPolls)) {
+                    set_device_status(status, QVX_ERR_TIMEOUT);
+                    late = true;
+                    break;
+                  }
+                  word = ld_relaxed_sys_u64(src);
+                }
+                v = __uint_as_float((uint32_t)word);
+              }
+              tot = q == 0 ? v : tot + v;
+            }
+            if (late) break;
+            __nv_bfloat16 yv = __float2bfloat16_rn(tot);
+            if (io.resid) yv = __float2bfloat16_rn(__bfloat162float(io.resid[e]) + __bfloat162float(yv));
+            y[e] = yv;
+          }
+      } else {
       const int p0 = r_begin >> 1, p1 = r_end >> 1;  // this CTA's row pairs
       const size_t nh = (size_t)(g.n_total >> 1);     // pairs per token row (one inbox half)
-      const size_t half = (size_t)(tag & 1u);
       for (int m = 0; m < mc; ++m) {
         const uint32_t* own = reinterpret_cast<const uint32_t*>(g.out[g.rank] + (size_t)(m0 + m) * g.n_total);
         for (int j = p0 + lane; j < p1; j += 32) {
@@ -410,6 +574,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
           }
         }
       }
+      }  // gather
       __syncwarp();
       if (lane == 0) {
         // count this CTA; the last one of the launch advances the slot's tag (every CTA has
@@ -427,13 +592,13 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
 
 template <int MC, int RT, bool FULLK, int S>
 static int launch_stream(int T, const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M,
-                         int N, int K, cudaStream_t stream, int* status, const QmvGather& g) {
+                         int N, int K, cudaStream_t stream, int* status, const QmvGather& g, const QmvIO& io) {
   auto kern = qmv_stream_kernel<MC, RT, FULLK, S>;
   const int P = (K + 1023) / 1024;
   const int threads = (T * P + 2) * 32;
   const int R = T * RT;
   const size_t stage = stream_stage_bytes(R, K);
-  const size_t smem = S * stage + 3 * S * sizeof(uint64_t) + 16;
+  const size_t smem = S * stage + 3 * S * sizeof(uint64_t) + 16 + kStreamRowSsBytes;
   static bool attr_set[64] = {};  // per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -461,7 +626,7 @@ static int launch_stream(int T, const void* x, const uint32_t* w, const void* s,
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const __nv_bfloat16*>(x), w,
                                      static_cast<const uint16_t*>(s), static_cast<const uint16_t*>(b),
-                                     static_cast<__nv_bfloat16*>(y), M, N, K, T, status, g);
+                                     static_cast<__nv_bfloat16*>(y), M, N, K, T, status, g, io);
   if (e != cudaSuccess) return fail(QVX_ERR_CUDA, "qvx_qmv launch: %s", cudaGetErrorString(e));
   return QVX_OK;
 }
@@ -469,10 +634,14 @@ static int launch_stream(int T, const void* x, const uint32_t* w, const void* s,
 // Returns QVX_OK after launching, or -1 when the streaming kernel does not apply
 // (the caller then uses the general kernel).
 int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* b, void* y, int M, int N, int K,
-                   cudaStream_t stream, const QmvGather* gather) {
+                   cudaStream_t stream, const QmvGather* gather, const QmvIO* in_out) {
   QmvGather g;
   memset(&g, 0, sizeof(g));
   if (gather) g = *gather;
+  QmvIO io;
+  memset(&io, 0, sizeof(io));
+  io.x_stride = K;
+  if (in_out) io = *in_out;
   if (K % 512 != 0 || K > kStreamMaxComputeWarps * 1024 || !aligned(s, 16) || !aligned(b, 16)) return -1;
   int* status = device_status_ptr();
   if (!status) return fail(QVX_ERR_CUDA, "qvx_qmv: device status word unavailable");
@@ -484,12 +653,12 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   while (rt > 1 && (size_t)T * rt * K / 2 > kStreamStageCodeBytes) rt /= 2;
   const bool fullk = K % 1024 == 0;
   // ring depth: as many stages (4..9) as the shared-memory budget holds
-  int depth = (int)((kStreamSmemBudget - 16) / (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)));
+  int depth = (int)((kStreamSmemBudget - 16 - kStreamRowSsBytes) / (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)));
   depth = depth < 4 ? 4 : depth > 9 ? 9 : depth;
 #define QVX_STREAM_S(MC_, RT_, S_)                                                                          \
   if (depth == S_)                                                                                          \
-    return fullk ? launch_stream<MC_, RT_, true, S_>(T, x, w, s, b, y, M, N, K, stream, status, g)             \
-                 : launch_stream<MC_, RT_, false, S_>(T, x, w, s, b, y, M, N, K, stream, status, g);
+    return fullk ? launch_stream<MC_, RT_, true, S_>(T, x, w, s, b, y, M, N, K, stream, status, g, io)         \
+                 : launch_stream<MC_, RT_, false, S_>(T, x, w, s, b, y, M, N, K, stream, status, g, io);
 #define QVX_STREAM_CASE(MC_, RT_)                                                                           \
   if (mc == MC_ && rt == RT_) {                                                                             \
     QVX_STREAM_S(MC_, RT_, 4)                                                                               \
@@ -551,9 +720,97 @@ extern "C" int qvx_qmv_allgather(const void* x, const uint32_t* w, const void* s
   d.n_total = g->n_total;
   d.row0 = g->row0;
   d.slot = g->slot;
-  rc = qmv_stream_try(x, w, scales, biases, g->out[g->rank], M, N, K, static_cast<cudaStream_t>(stream), &d);
+  d.mode = kExGather;
+  rc = qmv_stream_try(x, w, scales, biases, g->out[g->rank], M, N, K, static_cast<cudaStream_t>(stream), &d, nullptr);
   if (rc < 0)
     return fail(QVX_ERR_UNSUPPORTED, "qvx_qmv_allgather: needs K %% 512 == 0, K <= 12288 and 16-byte aligned "
                 "scales/biases (K=%d)", K);
+  return rc;
+}
+
+extern "C" int qvx_qmv_fused(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M,
+                             int N, int K, int group_size, int bits, const qvx_qmv_io* io, const qvx_gather* g,
+                             void* stream) {
+  using namespace qvx;
+  const char* who = "qvx_qmv_fused";
+  QmvIO d_io;
+  memset(&d_io, 0, sizeof(d_io));
+  d_io.x_stride = K;
+  if (io) {
+    d_io.in_mode = io->prologue;
+    d_io.x_stride = io->x_stride ? io->x_stride : (io->prologue == QVX_IN_SWIGLU ? 2LL * K : (long long)K);
+    d_io.norm_w = static_cast<const __nv_bfloat16*>(io->norm_w);
+    d_io.z = static_cast<const __nv_bfloat16*>(io->z);
+    d_io.z_stride = io->z_stride;
+    d_io.head_lanes = io->head_dim / 32;
+    d_io.eps = io->eps;
+    d_io.resid = static_cast<const __nv_bfloat16*>(io->resid);
+  }
+  if (d_io.in_mode < QVX_IN_PLAIN || d_io.in_mode > QVX_IN_GATED_RMS_NORM)
+    return fail(QVX_ERR_INVALID, "%s: unknown prologue %d", who, d_io.in_mode);
+  if (M < 1 || M > 8 || N < 1 || K < 512 || K % 512 != 0 || K > kStreamMaxComputeWarps * 1024)
+    return fail(QVX_ERR_INVALID, "%s: M=%d N=%d K=%d (M <= 8, K a multiple of 512 up to %d)", who, M, N, K,
+                kStreamMaxComputeWarps * 1024);
+  if (group_size != 64 || bits != 4)
+    return fail(QVX_ERR_UNSUPPORTED, "%s: group_size=%d bits=%d (64 and 4 supported)", who, group_size, bits);
+  if (!x || !w || !scales || !biases) return fail(QVX_ERR_INVALID, "%s: null pointer", who);
+  const long long need = d_io.in_mode == QVX_IN_SWIGLU ? 2LL * K : (long long)K;
+  if (d_io.x_stride < need || d_io.x_stride % 8 != 0 || !aligned(x, 16))
+    return fail(QVX_ERR_ALIGN, "%s: x needs 16-byte alignment and a row stride >= %lld, a multiple of 8 (got %lld)",
+                who, need, d_io.x_stride);
+  if (!aligned(w, 16) || !aligned(scales, 16) || !aligned(biases, 16))
+    return fail(QVX_ERR_ALIGN, "%s: w, scales and biases need 16-byte alignment", who);
+  if (d_io.in_mode == QVX_IN_RMS_NORM && (!d_io.norm_w || !aligned(d_io.norm_w, 16)))
+    return fail(QVX_ERR_INVALID, "%s: rms_norm prologue needs a 16-byte aligned norm weight of K values", who);
+  if (d_io.in_mode == QVX_IN_GATED_RMS_NORM) {
+    const int hl = d_io.head_lanes;
+    if (!d_io.norm_w || !d_io.z || !aligned(d_io.norm_w, 16) || !aligned(d_io.z, 16) || d_io.z_stride % 8 != 0 ||
+        d_io.z_stride < K || (hl != 1 && hl != 2 && hl != 4 && hl != 8 && hl != 16 && hl != 32) ||
+        K % io->head_dim != 0)
+      return fail(QVX_ERR_INVALID, "%s: gated rms_norm prologue: head_dim %d, z stride %lld (16-byte aligned z and "
+                  "weight, head_dim 32..1024 a power of two dividing K)", who, io->head_dim, d_io.z_stride);
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!g) {
+    if (!y || !aligned(y, 2)) return fail(QVX_ERR_INVALID, "%s: null or misaligned y", who);
+    const int rc = qmv_stream_try(x, w, scales, biases, y, M, N, K, s, nullptr, &d_io);
+    if (rc < 0) return fail(QVX_ERR_UNSUPPORTED, "%s: no streaming plan for K=%d", who, K);
+    return rc;
+  }
+  if (g->world < 1 || g->world > QVX_MAX_RANKS || g->rank < 0 || g->rank >= g->world || g->slot < 0)
+    return fail(QVX_ERR_INVALID, "%s: rank %d of world %d, slot %d", who, g->rank, g->world, g->slot);
+  for (int q = 0; q < g->world; ++q)
+    if (!g->inbox[q] || !aligned(g->inbox[q], 8)) return fail(QVX_ERR_INVALID, "%s: inbox of rank %d", who, q);
+  if (!g->epoch || !aligned(g->epoch, 4)) return fail(QVX_ERR_INVALID, "%s: missing epoch counters", who);
+  QmvGather d;
+  memset(&d, 0, sizeof(d));
+  for (int q = 0; q < g->world; ++q) {
+    d.out[q] = static_cast<__nv_bfloat16*>(g->out[q]);
+    d.inbox[q] = static_cast<unsigned long long*>(g->inbox[q]);
+  }
+  d.epoch = g->epoch;
+  d.world = g->world;
+  d.rank = g->rank;
+  d.n_total = g->n_total;
+  d.row0 = g->row0;
+  d.slot = g->slot;
+  if (g->mode == QVX_EXCHANGE_GATHER) {
+    if (d_io.resid) return fail(QVX_ERR_INVALID, "%s: the gather form has no residual epilogue", who);
+    if (N % 2 != 0 || (long long)g->n_total != (long long)g->world * N || g->row0 != g->rank * N ||
+        !g->out[g->rank] || !aligned(g->out[g->rank], 16))
+      return fail(QVX_ERR_INVALID, "%s: gather needs equal even shards in rank order and an aligned output", who);
+    d.mode = kExGather;
+    const int rc = qmv_stream_try(x, w, scales, biases, g->out[g->rank], M, N, K, s, &d, &d_io);
+    if (rc < 0) return fail(QVX_ERR_UNSUPPORTED, "%s: no streaming plan for K=%d", who, K);
+    return rc;
+  }
+  if (g->mode != QVX_EXCHANGE_REDUCE) return fail(QVX_ERR_INVALID, "%s: unknown exchange mode %d", who, g->mode);
+  if (g->n_total != N || g->row0 != 0 || !g->out[g->rank] || !aligned(g->out[g->rank], 16) || !y ||
+      N % 2 != 0)
+    return fail(QVX_ERR_INVALID, "%s: reduce needs n_total = N (even), row0 = 0, an aligned fp32 partial buffer in "
+                "out[rank] and an output y", who);
+  d.mode = kExReduce;
+  const int rc = qmv_stream_try(x, w, scales, biases, y, M, N, K, s, &d, &d_io);
+  if (rc < 0) return fail(QVX_ERR_UNSUPPORTED, "%s: no streaming plan for K=%d", who, K);
   return rc;
 }

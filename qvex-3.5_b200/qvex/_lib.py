@@ -34,6 +34,7 @@ SIGNATURES = {
     "qvx_qmm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "qvx_qmm_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_qmv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "qvx_qmv_fused": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "qvx_quantized_matmul": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "qvx_quantize": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_dequantize": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
@@ -61,7 +62,19 @@ class QvxGather(ctypes.Structure):
     (inboxes) of a column-sharded projection, this rank's launch counters, and its place in
     the rows."""
     _fields_ = [("out", _P * QVX_MAX_RANKS), ("inbox", _P * QVX_MAX_RANKS), ("epoch", _P),
-                ("world", _I), ("rank", _I), ("n_total", _I), ("row0", _I), ("slot", _I)]
+                ("world", _I), ("rank", _I), ("n_total", _I), ("row0", _I), ("slot", _I), ("mode", _I)]
+
+
+QVX_EXCHANGE_GATHER = 0
+QVX_EXCHANGE_REDUCE = 1
+QVX_IN_PLAIN, QVX_IN_RMS_NORM, QVX_IN_SWIGLU, QVX_IN_GATED_RMS_NORM = 0, 1, 2, 3
+
+
+class QvxQmvIO(ctypes.Structure):
+    """Mirror of ``qvx_qmv_io`` (include/qvex.h): the prologue and epilogue of a fused
+    decode projection."""
+    _fields_ = [("prologue", _I), ("x_stride", ctypes.c_longlong), ("norm_w", _P), ("z", _P),
+                ("z_stride", ctypes.c_longlong), ("head_dim", _I), ("eps", ctypes.c_float), ("resid", _P)]
 
 
 class QvexError(RuntimeError):

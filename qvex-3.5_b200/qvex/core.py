@@ -165,3 +165,56 @@ def dequantize_rows(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                                     flat.numel(), _ptr(out), N, K, group_size, bits, _stream(w)),
           "qvx_dequantize_rows")
     return out
+
+
+_PROLOGUES = {"plain": _lib.QVX_IN_PLAIN, "rms_norm": _lib.QVX_IN_RMS_NORM, "swiglu": _lib.QVX_IN_SWIGLU,
+              "gated_rms_norm": _lib.QVX_IN_GATED_RMS_NORM}
+
+
+def _rows(t: torch.Tensor, name: str) -> torch.Tensor:
+    t2 = t.reshape(-1, t.shape[-1]) if t.dim() != 2 else t
+    if t2.stride(-1) != 1:
+        raise ValueError(f"{name} must have unit stride along its rows")
+    return t2
+
+
+def qmv_fused(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
+              prologue: str = "plain", norm_w: torch.Tensor | None = None, z: torch.Tensor | None = None,
+              head_dim: int = 0, eps: float = 1e-6, resid: torch.Tensor | None = None,
+              out: torch.Tensor | None = None, gather=None, group_size: int = 64, bits: int = 4) -> torch.Tensor:
+    """Decode projection (M <= 8 token rows) with a fused prologue and residual epilogue
+    (qvx_qmv_fused):  y = resid + (prologue(x) @ dequant(w)^T)  (resid optional), where the
+    prologue is "plain", "rms_norm" (norm_w [K]), "swiglu" (x = gate|up rows of 2K) or
+    "gated_rms_norm" (per head of head_dim, norm_w [head_dim], z rows).  ``gather`` is a
+    qvx_gather descriptor (ctypes) for the sharded forms.  Returns y [M, N] (``out``)."""
+    _check_qparams(group_size, bits)
+    if prologue not in _PROLOGUES:
+        raise ValueError(f"prologue must be one of {sorted(_PROLOGUES)}")
+    _require_cuda("x", x, (torch.bfloat16,))
+    w = _packed(w)
+    N, KW = w.shape
+    K = KW * 32 // bits
+    x2 = _rows(x, "x")
+    M = x2.shape[0]
+    io = _lib.QvxQmvIO()
+    io.prologue = _PROLOGUES[prologue]
+    io.x_stride = x2.stride(0)
+    io.eps = float(eps)
+    if norm_w is not None:
+        io.norm_w = norm_w.data_ptr()
+    if z is not None:
+        z2 = _rows(z, "z")
+        io.z, io.z_stride = z2.data_ptr(), z2.stride(0)
+    io.head_dim = int(head_dim)
+    if resid is not None:
+        r2 = _rows(resid, "resid")
+        if tuple(r2.shape) != (M, N) or not r2.is_contiguous():
+            raise ValueError("resid must be a contiguous [M, N] bf16 tensor")
+        io.resid = r2.data_ptr()
+    if out is None and not (gather is not None and gather.mode == _lib.QVX_EXCHANGE_GATHER):
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    import ctypes
+    check(lib().qvx_qmv_fused(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
+                              ctypes.byref(io), ctypes.byref(gather) if gather is not None else None, _stream(x2)),
+          "qvx_qmv_fused")
+    return out

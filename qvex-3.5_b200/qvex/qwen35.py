@@ -32,7 +32,7 @@ from pathlib import Path
 import torch
 
 from . import glue
-from .core import dequantize_rows
+from .core import dequantize_rows, qmv_fused
 from .kernels import gated_delta
 from .model import QEmbedding, QLinear, RecurrentCache
 
@@ -151,6 +151,11 @@ def _qlin(p) -> QLinear:
     return p if isinstance(p, QLinear) else QLinear(*p)
 
 
+def _fused(lin: QLinear, x: torch.Tensor, prologue: str, **kw) -> torch.Tensor:
+    return qmv_fused(x, lin.w, lin.scales, lin.biases, prologue=prologue, group_size=lin.group_size, bits=lin.bits,
+                     **kw)
+
+
 class Attention:
     """Gated full attention (engine/model.py:199-232)."""
 
@@ -176,8 +181,12 @@ class Attention:
     def mix(self, x: torch.Tensor, cache: KVCache, pos=None) -> torch.Tensor:
         """The o_proj input [B, L, H*D] (everything of __call__ but o_proj).  ``pos`` (a device
         int32 tensor) overrides cache.offset for CUDA-graph decode."""
-        B, L, _ = x.shape
-        qkv = self.qkv(x)
+        return self.attend(self.qkv(x), cache, pos)
+
+    def attend(self, qkv: torch.Tensor, cache: KVCache, pos=None) -> torch.Tensor:
+        """From the fused q|k|v projection output [B, L, *] to the o_proj input."""
+        B, L, _ = qkv.shape
+        x = qkv
         cache.reserve(B, self.n_kv, self.head_dim, L, x.device)
         G = self.n_heads // self.n_kv
         ws, ns = None, 0
@@ -227,6 +236,15 @@ class GatedDeltaNet:
         form a CUDA graph replays); otherwise new tensors replace them, as in the reference."""
         B, S, _ = x.shape
         proj = self.in_proj(x)
+        y = self.recur(proj, cache, keep_prev, inplace)
+        z = proj.view(B * S, -1)[:, self.conv_dim:self.conv_dim + self.value_dim]
+        return glue.gated_rms_norm(y, z, self.norm_w, self.cfg.rms_norm_eps).view(B, S, self.value_dim)
+
+    def recur(self, proj: torch.Tensor, cache: RecurrentCache, keep_prev: bool = False,
+              inplace: bool = False) -> torch.Tensor:
+        """From the in_proj output [B, S, *] to the recurrence output y [B, S, Hv, Dv]."""
+        B, S, _ = proj.shape
+        x = proj
         if cache.conv is None:
             self.init_state(cache, B, x.device)
         r = glue.deltanet_conv(proj, self.conv_w, cache.conv, self.hk, self.hv, self.dk, self.dv, keep_mid=keep_prev,
@@ -240,8 +258,7 @@ class GatedDeltaNet:
         if keep_prev:
             cache.ssm_prev = g[2]
         cache.offset += S
-        z = proj.view(B * S, -1)[:, self.conv_dim:self.conv_dim + self.value_dim]
-        return glue.gated_rms_norm(y, z, self.norm_w, self.cfg.rms_norm_eps).view(B, S, self.value_dim)
+        return y
 
     def __call__(self, x: torch.Tensor, cache: RecurrentCache, keep_prev: bool = False) -> torch.Tensor:
         return self.out_proj(self.mix(x, cache, keep_prev))
@@ -268,6 +285,8 @@ class Layer:
         self.mlp = MLP(p["mlp"])
         self.ln1, self.ln2 = p["input_layernorm"], p["post_attention_layernorm"]
         self.eps = cfg.rms_norm_eps
+        self.tp = None        # qvex.tp.TP when the layer is one rank's shard
+        self.tp_desc = None   # (mixer output, MLP down) reduce descriptors for fused decode
 
     def _mixer(self, n, cache, keep_prev, pos=None):
         if self.linear:
@@ -286,12 +305,45 @@ class Layer:
         else:
             n, x = glue.rms_norm(pending, self.ln1, self.eps, resid=x)
         m = self._mixer(n, cache, keep_prev, pos)
+        if self.tp is not None:
+            self.tp.all_reduce(m)   # row-parallel out_proj / o_proj: sum the ranks' partials
         n2, h = glue.rms_norm(m, self.ln2, self.eps, resid=x)
-        return h, self.mlp(n2)
+        mo = self.mlp(n2)
+        if self.tp is not None:
+            self.tp.all_reduce(mo)  # row-parallel down_proj
+        return h, mo
 
     def __call__(self, x: torch.Tensor, cache, keep_prev: bool = False) -> torch.Tensor:
         h, mo = self.forward_deferred(x, None, cache, keep_prev)
         return glue.add(h, mo)
+
+    def forward_fused(self, x: torch.Tensor, cache, pos: torch.Tensor) -> None:
+        """Decode form (B <= 8 tokens, one per sequence): the residual stream x [B, 1, H] is
+        updated in place, every norm, SwiGLU and residual add riding in the projections'
+        prologues and epilogues (qvx_qmv_fused).  Gives the same bits as forward_deferred."""
+        B = x.shape[0]
+        x2 = x.view(B, -1)
+        mx = self.mixer
+        # sharded: the row-parallel projections sum their partials across the ranks in-kernel
+        red_mix, red_down = self.tp_desc if self.tp_desc is not None else (None, None)
+        if self.linear:
+            proj = _fused(mx.in_proj, x2, "rms_norm", norm_w=self.ln1, eps=self.eps)
+            y = mx.recur(proj.view(B, 1, -1), cache, inplace=True)
+            z = proj[:, mx.conv_dim:mx.conv_dim + mx.value_dim]
+            _fused(mx.out_proj, y.view(B, -1), "gated_rms_norm", norm_w=mx.norm_w, z=z, head_dim=mx.dv,
+                   eps=self.eps, resid=x2, out=x2, gather=red_mix)
+        else:
+            qkv = _fused(mx.qkv, x2, "rms_norm", norm_w=self.ln1, eps=self.eps)
+            o = mx.attend(qkv.view(B, 1, -1), cache, pos)
+            _fused(mx.o_proj, o.view(B, -1), "plain", resid=x2, out=x2, gather=red_mix)
+        gu = _fused(self.mlp.gate_up, x2, "rms_norm", norm_w=self.ln2, eps=self.eps)
+        _fused(self.mlp.down, gu, "swiglu", resid=x2, out=x2, gather=red_down)
+
+    def fusable(self, B: int) -> bool:
+        """Whether forward_fused applies: B <= 8 and every projection's K a multiple of 512."""
+        lins = [self.mlp.gate_up, self.mlp.down] + (
+            [self.mixer.in_proj, self.mixer.out_proj] if self.linear else [self.mixer.qkv, self.mixer.o_proj])
+        return B <= 8 and all(l.in_features % 512 == 0 and l.group_size == 64 and l.bits == 4 for l in lins)
 
 
 class Qwen35:
@@ -300,6 +352,14 @@ class Qwen35:
     def __init__(self, cfg: Config, embed: QEmbedding, layers: list[Layer], norm: torch.Tensor, lm_head: QLinear):
         self.cfg = cfg
         self.embed, self.layers, self.norm, self.lm_head = embed, layers, norm, lm_head
+        self.tp = None       # qvex.tp.TP when this is one rank's shard (qvex.tp.attach)
+        self.lm_desc = None  # gather descriptor of lm_head for fused decode (sharded)
+
+    def _logits(self, n: torch.Tensor) -> torch.Tensor:
+        y = self.lm_head(n)
+        if self.tp is not None:
+            y = self.tp.all_gather_cols(y)  # vocabulary rows of every rank, in rank order
+        return y
 
     def make_cache(self, capacity: int | None = None):
         return [RecurrentCache() if l.linear else KVCache(capacity) for l in self.layers]
@@ -325,13 +385,28 @@ class Qwen35:
                     raise ValueError("graph decode needs KV caches of fixed capacity (make_cache(capacity))")
                 c.reserve(B, layer.mixer.n_kv, layer.mixer.head_dim, 0, device)
 
-    def decode_step(self, ids: torch.Tensor, cache, pos: torch.Tensor) -> torch.Tensor:
+    def decode_step(self, ids: torch.Tensor, cache, pos: torch.Tensor, fused: bool | None = None) -> torch.Tensor:
         """One decode step of B sequences, ids [B, 1] int32 at the device position ``pos``
         (int32 [1]): every state updated in its own buffer and nothing read on the host, so the
-        step can be captured once and replayed for every token.  Returns logits [B, 1, V]."""
-        x, pending = self.hidden(ids, cache, pos=pos)
-        n = glue.rms_norm(pending, self.norm, self.cfg.rms_norm_eps, resid=x)[0]
-        return self.lm_head(n)
+        step can be captured once and replayed for every token.  Returns logits [B, 1, V].
+        With ``fused`` (default: wherever it applies, B <= 8) the norms, SwiGLU and residual
+        adds ride in the projection kernels (same bits, fewer launches)."""
+        B = ids.shape[0]
+        if fused is None:
+            fused = all(l.fusable(B) for l in self.layers) and self.lm_head.in_features % 512 == 0
+        if not fused:
+            x, pending = self.hidden(ids, cache, pos=pos)
+            n = glue.rms_norm(pending, self.norm, self.cfg.rms_norm_eps, resid=x)[0]
+            return self._logits(n)
+        x = self.embed(ids)  # [B, 1, H], the residual stream, updated in place below
+        for layer, c in zip(self.layers, cache):
+            layer.forward_fused(x, c, pos)
+        if self.lm_desc is not None:  # sharded: vocabulary rows gathered inside the kernel
+            _fused(self.lm_head, x.view(B, -1), "rms_norm", norm_w=self.norm, eps=self.cfg.rms_norm_eps,
+                   gather=self.lm_desc)
+            return self.tp.peer.output(self.lm_desc.slot, B, self.lm_desc.n_total).view(B, 1, -1)
+        return _fused(self.lm_head, x.view(B, -1), "rms_norm", norm_w=self.norm,
+                      eps=self.cfg.rms_norm_eps).view(B, 1, -1)
 
     def __call__(self, ids: torch.Tensor, cache, last_only: bool = True, return_hidden: bool = False,
                  keep_prev: bool = False):
@@ -340,11 +415,11 @@ class Qwen35:
         if last_only and not return_hidden:
             n = glue.rms_norm(pending[:, -1:].contiguous(), self.norm, self.cfg.rms_norm_eps,
                               resid=x[:, -1:].contiguous())[0]
-            return self.lm_head(n)
+            return self._logits(n)
         n, h = glue.rms_norm(pending, self.norm, self.cfg.rms_norm_eps, resid=x)
         if last_only:
             n = n[:, -1:].contiguous()
-        logits = self.lm_head(n)
+        logits = self._logits(n)
         return (logits, h) if return_hidden else logits
 
     # ------------------------------------------------------------ random initialisation
@@ -477,6 +552,7 @@ class DecodeGraph:
         # warm-up outside the graph (module loads, launch attributes, workspaces), then undo
         # its state changes so the graph starts from the caller's state
         saved = [(c.conv.clone(), c.ssm.clone()) if isinstance(c, RecurrentCache) else None for c in cache]
+        offsets = [c.offset for c in cache]
         ids0 = self.ids.clone()
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
@@ -489,11 +565,10 @@ class DecodeGraph:
                 c.ssm.copy_(sv[1])
         self.ids.copy_(ids0)
         self.pos.fill_(pos)
-        offsets = [c.offset for c in cache]
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self.logits = step()
-        for c, o in zip(cache, offsets):  # capture ran the Python side once more
+        for c, o in zip(cache, offsets):  # warm-up and capture ran the Python side twice
             c.offset = o
 
     def replay(self) -> None:

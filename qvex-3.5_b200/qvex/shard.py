@@ -93,12 +93,11 @@ GATHER_ALIGN = 256
 GATHER_M_MAX = 8  # tokens a fused decode projection gathers (qvx_qmv's M <= 8)
 
 
-def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], list[int], int]:
-    """Byte layout of one rank's PeerGather buffer: per slot, the full output (``region_bytes``
-    of bf16) and then its inbox (four times that: one 64-bit word, two outputs and a tag,
-    per output pair, in two halves that alternating launches use), each 256-byte aligned.
-    Returns the outputs' offsets, the inboxes' offsets and the total size."""
-    if any(b <= 0 for b in region_bytes):
+def plan_layout(sizes: list[tuple[int, int]]) -> tuple[list[int], list[int], int]:
+    """Byte layout of one rank's PeerGather buffer from (output bytes, inbox bytes) per slot:
+    the output and then the inbox, each 256-byte aligned.  Returns the outputs' offsets, the
+    inboxes' offsets and the total size."""
+    if any(o <= 0 or i <= 0 for o, i in sizes):
         raise ValueError("every region needs a positive size")
 
     def up(v):
@@ -106,12 +105,25 @@ def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], list[int], i
 
     at = 0
     outs, inboxes = [], []
-    for b in region_bytes:
+    for o, i in sizes:
         outs.append(at)
-        at = up(at + b)
+        at = up(at + o)
         inboxes.append(at)
-        at = up(at + 4 * b)
+        at = up(at + i)
     return outs, inboxes, at
+
+
+def plan_gather_layout(region_bytes: list[int]) -> tuple[list[int], list[int], int]:
+    """Layout of gather slots only: per slot the full output (``region_bytes`` of bf16) and
+    its inbox, four times that (one 64-bit word, two outputs and a tag, per output pair, in
+    two halves that alternating launches use)."""
+    return plan_layout([(b, 4 * b) for b in region_bytes])
+
+
+def reduce_slot_bytes(m_max: int, n: int, world: int) -> tuple[int, int]:
+    """(partial-sum bytes, inbox bytes) of a row-parallel reduce slot: fp32 partials [m_max, n];
+    an inbox of 64-bit (fp32, tag) words [2 halves][world][m_max][n]."""
+    return 4 * m_max * n, 2 * world * m_max * n * 8
 
 
 def gather_descriptor(bases: list[int], out_offset: int, inbox_offset: int, epoch_ptr: int, rank: int,
@@ -152,7 +164,9 @@ class PeerGather:
     construct it with the same list, and keep it alive while its projections are in use.
     Set-up allocates and exchanges handles; the projections themselves allocate nothing."""
 
-    def __init__(self, region_bytes: list[int], group=None):
+    def __init__(self, region_bytes: list[int], group=None, reduce: list[tuple[int, int]] | None = None):
+        """``region_bytes``: one bf16 output size per gather slot; ``reduce``: (m_max, n) per
+        row-parallel reduce slot (numbered after the gather slots)."""
         from cuda.bindings import runtime as rt
         from . import _lib
         self._rt = rt
@@ -163,8 +177,13 @@ class PeerGather:
             raise ValueError(f"{self.world} ranks; the fused gather supports up to {_lib.QVX_MAX_RANKS}")
         self.device = torch.cuda.current_device()
         _ck(rt.cudaSetDevice(self.device))
-        self.offsets, self.inboxes, self.nbytes = plan_gather_layout(region_bytes)
-        self.slots = len(region_bytes)
+        reduce = list(reduce or [])
+        self.reduce_shapes = reduce
+        self.n_gather = len(region_bytes)
+        sizes = [(b, 4 * b) for b in region_bytes] + [reduce_slot_bytes(m, n, self.world) for m, n in reduce]
+        self.offsets, self.inboxes, self.nbytes = plan_layout(sizes)
+        self.slots = len(sizes)
+        self._next_reduce = self.n_gather
         self._own = _ck(rt.cudaMalloc(self.nbytes))
         _ck(rt.cudaMemset(self._own, 0, self.nbytes))
         _ck(rt.cudaDeviceSynchronize())
@@ -184,11 +203,30 @@ class PeerGather:
         dist.barrier(group)  # every rank has mapped every buffer before anyone stores
 
     def reserve(self) -> int:
-        """Hands out the next slot."""
-        if self._next >= self.slots:
-            raise ValueError(f"all {self.slots} gather slots are taken")
+        """Hands out the next gather slot."""
+        if self._next >= self.n_gather:
+            raise ValueError(f"all {self.n_gather} gather slots are taken")
         self._next += 1
         return self._next - 1
+
+    def reserve_reduce(self) -> int:
+        """Hands out the next reduce slot."""
+        if self._next_reduce >= self.slots:
+            raise ValueError(f"all {self.slots - self.n_gather} reduce slots are taken")
+        self._next_reduce += 1
+        return self._next_reduce - 1
+
+    def reduce_descriptor(self, slot: int, n: int):
+        """qvx_gather (mode QVX_EXCHANGE_REDUCE) of a reduce slot: out[rank] = this rank's fp32
+        partial sums, inbox[r] = rank r's receive area, n_total = n, row0 = 0."""
+        from . import _lib
+        m_max, n_max = self.reduce_shapes[slot - self.n_gather]
+        if n > n_max:
+            raise ValueError(f"reduce slot {slot} holds {n_max} rows, not {n}")
+        d = gather_descriptor(self.base, self.offsets[slot], self.inboxes[slot], self.epoch.data_ptr(), self.rank,
+                              slot, n, 0)
+        d.mode = _lib.QVX_EXCHANGE_REDUCE
+        return d
 
     def descriptor(self, slot: int, n_total: int, row0: int):
         return gather_descriptor(self.base, self.offsets[slot], self.inboxes[slot], self.epoch.data_ptr(),
