@@ -60,7 +60,7 @@ def parse_args():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the config-2/3 kernel measurements (prefill qmm, quantize, gated DeltaNet)")
     ap.add_argument("--profile", nargs="?", const="step", default=None,
-                    choices=["step", "qmm", "qmm_small", "quantize", "gd_prefill", "gd_decode"],
+                    choices=["step", "qmm", "qmm_small", "quantize", "gd_prefill", "gd_decode", "model_decode"],
                     help="run one case eagerly for a profiler (no graph, clocks or CPU baseline)")
     return ap.parse_args()
 
@@ -246,8 +246,32 @@ def measure_model(torch, device, peak_gbs, decode_steps=256, prefill=4096, batch
 
 
 def profile_case(torch, device, case, reps):
-    """One eagerly-launched case for ncu (small enough for a full-section capture)."""
+    """One eagerly-launched case for ncu (small enough for a full-section capture).
+    model_decode: prefill 4096 tokens outside the profiler range, then `reps` eager decode
+    steps of the 9B-shaped model inside it (ncu --profile-from-start off)."""
     import qvex
+    if case == "model_decode":
+        from qvex.qwen35 import Config, Qwen35
+        cfg = Config.qwen35_9b()
+        model = Qwen35.random(cfg, seed=0, device=device)
+        cache = model.make_cache(capacity=4096 + reps + 8)
+        g = torch.Generator(device=device)
+        g.manual_seed(5)
+        ids = torch.randint(0, cfg.vocab_size, (1, 4096), device=device, generator=g, dtype=torch.int64).to(torch.int32)
+        for c0 in range(0, 4096, 512):
+            model(ids[:, c0:c0 + 512].contiguous(), cache, last_only=True)
+        model.prepare_decode(cache, 1, device)
+        pos = torch.tensor([4096], dtype=torch.int32, device=device)
+        tok = ids[:, -1:].contiguous()
+        model.decode_step(tok, cache, pos)  # warm (module loads) outside the range
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        for _ in range(reps):
+            model.decode_step(tok, cache, pos)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profile_run": case, "reps": reps}))
+        return
     if case in ("qmm", "qmm_small"):
         c = config_cases(torch, device, small=(case == "qmm_small"))
         for _ in range(reps):
