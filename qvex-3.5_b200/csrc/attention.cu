@@ -22,7 +22,7 @@
 //                        eight queries per warp, keys walked in order with a running max.
 // Positions come from a host value or, for a CUDA graph replayed at every position, from an
 // int32 in device memory.
-#include "common.cuh"
+#include "sm100.cuh"
 
 namespace qvx {
 
@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(128) attn_prep_kernel(const __nv_bfloat16* __r
 
 constexpr int kAttnMaxQ = 8;    // queries per KV head in the decode kernel
 constexpr int kAttnWarps = 4;
+constexpr int kAttnTile = 64;   // keys per shared-memory tile
 
 template <int NPT>
 __device__ __forceinline__ float gate_sigmoid_bf16(const __nv_bfloat16* row, int h, int d) {
@@ -109,134 +110,200 @@ __device__ __forceinline__ float gate_sigmoid_bf16(const __nv_bfloat16* row, int
   return __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-g))));
 }
 
-// grid (nsplit, Hkv, B); GL = G * L queries; workspace: partials [B, Hkv, nsplit, GL, D + 2]
-// fp32 then counters [B * Hkv] int32 (zero before the first call; the kernel leaves them at zero)
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// 32 values per lane -> lane l holds the warp-wide sum of value l (a transposing butterfly:
+// at offset o the lanes with bit o set keep the upper half of the remaining values, so value
+// index bit k ends up equal to lane bit k; 31 shuffles for 32 sums instead of 160)
+__device__ __forceinline__ float reduce32_transpose(float (&p)[32], int lane) {
+#pragma unroll
+  for (int off = 16, n = 32; off >= 1; off >>= 1, n >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = up ? p[i] : p[i + n / 2];
+      const float keep = up ? p[i + n / 2] : p[i];
+      p[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return p[0];
+}
+
+// grid (nsplit, Hkv, B), 128 threads; dynamic shared memory: K and V tiles (double
+// buffered), the tile's scores.  Workspace: partials [B, Hkv, nsplit, GL, D + 2] fp32, then
+// counters [B * Hkv] int32 (zero before the first call; the kernel leaves them at zero).
+//
+// Per 64-key tile: cp.async brings the K and V rows (contiguous in the cache) into shared
+// memory while the previous tile is used; warp w forms the q.k dots of keys
+// [16w, 16w + 16) for all GL queries with lane l holding features [l*D/32, ...) of each
+// (conflict-free row reads), reduced by a transposing butterfly; a running max / sum per
+// query rescales the outputs; thread t accumulates output features {t, t + 128, ...} of
+// every query over the tile's keys.
 template <int NPT, int GL>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* k_cache,
     const __nv_bfloat16* v_cache, __nv_bfloat16* __restrict__ out, float* __restrict__ part, int* __restrict__ count,
     const int* pos_dev, int pos_host, AttnShape sh) {
   constexpr int D = NPT * 32;
-  __shared__ float qs[GL][D];
-  __shared__ float wm[kAttnWarps][GL], wl[kAttnWarps][GL];
-  __shared__ float wo[kAttnWarps][GL][D];
+  constexpr int KT = kAttnTile;
+  constexpr int DPT = D >= 128 ? D / 128 : 1;  // output features per thread
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(attn_smem);   // [2][KT][D]
+  __nv_bfloat16* Vs = Ks + 2 * KT * D;                                // [2][KT][D]
+  float* ps = reinterpret_cast<float*>(Vs + 2 * KT * D);              // [GL][KT]
+  __shared__ float alpha_s[GL], m_s[GL], l_s[GL];
   __shared__ int is_last;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x, nsplit = gridDim.x, kvh = blockIdx.y, bi = blockIdx.z;
   const int G = sh.H / sh.Hkv;
   const int pos0 = attn_pos0(pos_dev, pos_host);
   const int nkeys = pos0 + sh.L;
-  // this CTA's keys: ranges of a multiple of 32 keys
-  const int per = ((nkeys + nsplit - 1) / nsplit + 31) & ~31;
+  const int per = ((nkeys + nsplit - 1) / nsplit + KT - 1) / KT * KT;
   const int j0 = split * per, j1 = min(nkeys, j0 + per);
+  const int ntiles = j1 > j0 ? (j1 - j0 + KT - 1) / KT : 0;
 
-  for (int i = threadIdx.x; i < GL * D; i += blockDim.x) {
-    const int g = i / D, d = i % D;
-    const int t = g / G, hq = kvh * G + g % G;
-    qs[g][d] = t < sh.L ? __bfloat162float(q[(((size_t)bi * sh.L + t) * sh.H + hq) * D + d]) : 0.0f;
-  }
-  __syncthreads();
-
-  const __nv_bfloat16* kc = k_cache + ((size_t)bi * sh.Hkv + kvh) * sh.cap * D;
-  const __nv_bfloat16* vc = v_cache + ((size_t)bi * sh.Hkv + kvh) * sh.cap * D;
-  float m[GL], l[GL], o[GL][NPT];
+  // this lane's features of every query (zeros for padding queries)
+  float qv[GL][NPT];
 #pragma unroll
   for (int g = 0; g < GL; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.0f;
+    const int t = g / G, hq = kvh * G + g % G;
+    const bool live = g < G * sh.L;
 #pragma unroll
-    for (int i = 0; i < NPT; ++i) o[g][i] = 0.0f;
+    for (int i = 0; i < NPT; ++i)
+      qv[g][i] = live ? __bfloat162float(q[(((size_t)bi * sh.L + t) * sh.H + hq) * D + lane * NPT + i]) : 0.0f;
   }
-  // warps take 32-key blocks of the range in turn
-  for (int jb = j0 + warp * 32; jb < j1; jb += kAttnWarps * 32) {
-    const int j = jb + lane;
-    float s[GL];
-#pragma unroll
-    for (int g = 0; g < GL; ++g) s[g] = 0.0f;
-    if (j < j1) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)j * D);
-#pragma unroll 4
-      for (int c = 0; c < D / 8; ++c) {
-        const uint4 kv = __ldg(kr + c);
-        const uint32_t u[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float k0 = __uint_as_float(u[e] << 16), k1 = __uint_as_float(u[e] & 0xffff0000u);
-#pragma unroll
-          for (int g = 0; g < GL; ++g) s[g] = fmaf(qs[g][8 * c + 2 * e + 1], k1, fmaf(qs[g][8 * c + 2 * e], k0, s[g]));
-        }
-      }
-    }
-    float pj[GL];
-#pragma unroll
-    for (int g = 0; g < GL; ++g) {
-      const int t = g / G;
-      const bool ok = j < j1 && g < G * sh.L && j <= pos0 + t;  // causal within the new tokens
-      s[g] = ok ? s[g] * sh.scale : -INFINITY;
-      float mx = s[g];
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mn = fmaxf(m[g], mx);
-      // nothing seen yet for this query (mn = -inf): leave its state alone
-      const float alpha = mn == -INFINITY ? 1.0f : expf(m[g] - mn);
-      pj[g] = mn == -INFINITY ? 0.0f : expf(s[g] - mn);
-      float ps = pj[g];
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-      l[g] = l[g] * alpha + ps;
-      m[g] = mn;
-#pragma unroll
-      for (int i = 0; i < NPT; ++i) o[g][i] *= alpha;
-    }
-    // each value row once for all queries
-    const int jn = min(32, j1 - jb);
-    for (int jj = 0; jj < jn; ++jj) {
-      float vv[NPT];
-      const __nv_bfloat16* vr = vc + (size_t)(jb + jj) * D + lane * NPT;
-#pragma unroll
-      for (int i = 0; i < NPT; ++i) vv[i] = __bfloat162float(vr[i]);
-#pragma unroll
-      for (int g = 0; g < GL; ++g) {
-        const float pb = __shfl_sync(0xffffffffu, pj[g], jj);
-#pragma unroll
-        for (int i = 0; i < NPT; ++i) o[g][i] = fmaf(pb, vv[i], o[g][i]);
-      }
-    }
+  if (tid < GL) {
+    m_s[tid] = -INFINITY;
+    l_s[tid] = 0.0f;
   }
-  // merge the warps
-  if (lane == 0)
-#pragma unroll
-    for (int g = 0; g < GL; ++g) {
-      wm[warp][g] = m[g];
-      wl[warp][g] = l[g];
-    }
+  __syncthreads();
+  float o[GL][DPT];
 #pragma unroll
   for (int g = 0; g < GL; ++g)
 #pragma unroll
-    for (int i = 0; i < NPT; ++i) wo[warp][g][lane * NPT + i] = o[g][i];
-  __syncthreads();
-  float* my = part + ((((size_t)bi * sh.Hkv + kvh) * nsplit + split) * GL) * (D + 2);
-  for (int i = threadIdx.x; i < GL * D; i += blockDim.x) {
-    const int g = i / D, d = i % D;
-    float mm = -INFINITY;
-    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, wm[w][g]);
-    float ll = 0.0f, oo = 0.0f;
-    if (mm != -INFINITY)
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float f = expf(wm[w][g] - mm);
-        ll = fmaf(wl[w][g], f, ll);
-        oo = fmaf(wo[w][g][d], f, oo);
+    for (int i = 0; i < DPT; ++i) o[g][i] = 0.0f;
+
+  const __nv_bfloat16* kc = k_cache + ((size_t)bi * sh.Hkv + kvh) * sh.cap * D;
+  const __nv_bfloat16* vc = v_cache + ((size_t)bi * sh.Hkv + kvh) * sh.cap * D;
+  auto load_tile = [&](int i, int buf) {
+    const int t0 = j0 + i * KT, rows = min(KT, j1 - t0);
+    const int chunks = rows * D / 8;  // 16-byte pieces per matrix
+    for (int c = tid; c < chunks; c += blockDim.x) {
+      cp_async16(Ks + (size_t)buf * KT * D + c * 8, kc + (size_t)t0 * D + c * 8);
+      cp_async16(Vs + (size_t)buf * KT * D + c * 8, vc + (size_t)t0 * D + c * 8);
+    }
+    cp_async_commit();
+  };
+  if (ntiles > 0) load_tile(0, 0);
+  for (int it = 0; it < ntiles; ++it) {
+    const int buf = it & 1;
+    if (it + 1 < ntiles) {
+      load_tile(it + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int t0 = j0 + it * KT, rows = min(KT, j1 - t0);
+    const __nv_bfloat16* Kt = Ks + (size_t)buf * KT * D;
+    const __nv_bfloat16* Vt = Vs + (size_t)buf * KT * D;
+    // scores of keys [16 warp, 16 warp + 16): up to 32 (key, query) sums per round
+    constexpr int KPR = 32 / GL > 16 ? 16 : 32 / GL;  // keys per reduction round
+#pragma unroll
+    for (int kb = 0; kb < 16; kb += KPR) {
+      float pv[32];
+#pragma unroll
+      for (int i = KPR * GL; i < 32; ++i) pv[i] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < KPR; ++kk) {
+        const int j = warp * 16 + kb + kk;
+        float kf[NPT];
+#pragma unroll
+        for (int i = 0; i < NPT; ++i) kf[i] = __bfloat162float(Kt[(size_t)j * D + lane * NPT + i]);
+#pragma unroll
+        for (int g = 0; g < GL; ++g) {
+          float d = 0.0f;
+#pragma unroll
+          for (int i = 0; i < NPT; ++i) d = fmaf(qv[g][i], kf[i], d);
+          pv[kk * GL + g] = d;
+        }
       }
-    my[(size_t)g * (D + 2) + 2 + d] = oo;
-    if (d == 0) {
-      my[(size_t)g * (D + 2)] = mm;
-      my[(size_t)g * (D + 2) + 1] = ll;
+      const float sum = reduce32_transpose(pv, lane);
+      // lane l now holds value index l = kk * GL + g (lanes past KPR * GL hold padding)
+      if (lane < KPR * GL) {
+        const int kk = lane / GL, g = lane % GL;
+        const int j = warp * 16 + kb + kk;
+        const int t = g / G;
+        const bool ok = j < rows && g < G * sh.L && t0 + j <= pos0 + t;  // causal within the new tokens
+        ps[g * KT + j] = ok ? sum * sh.scale : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // running max and sum per query (warp g % 4 handles query g)
+    for (int g = warp; g < GL; g += kAttnWarps) {
+      const float s0 = ps[g * KT + lane], s1 = ps[g * KT + 32 + lane];
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mo = m_s[g];
+      const float mn = fmaxf(mo, mx);
+      const float p0 = mn == -INFINITY ? 0.0f : expf(s0 - mn), p1 = mn == -INFINITY ? 0.0f : expf(s1 - mn);
+      ps[g * KT + lane] = p0;
+      ps[g * KT + 32 + lane] = p1;
+      float sm = p0 + p1;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+      __syncwarp();
+      if (lane == 0) {
+        const float a = mn == -INFINITY ? 1.0f : expf(mo - mn);
+        alpha_s[g] = a;
+        l_s[g] = l_s[g] * a + sm;
+        m_s[g] = mn;
+      }
+    }
+    __syncthreads();
+    // outputs: thread tid owns features tid, tid + 128, ...
+#pragma unroll
+    for (int i = 0; i < DPT; ++i) {
+      const int d = tid + 128 * i;
+      if (d < D) {
+        float acc[GL];
+#pragma unroll
+        for (int g = 0; g < GL; ++g) acc[g] = o[g][i] * alpha_s[g];
+        for (int j = 0; j < rows; ++j) {
+          const float vv = __bfloat162float(Vt[(size_t)j * D + d]);
+#pragma unroll
+          for (int g = 0; g < GL; ++g) acc[g] = fmaf(ps[g * KT + j], vv, acc[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < GL; ++g) o[g][i] = acc[g];
+      }
+    }
+    __syncthreads();  // the tile's buffers and scores are free again
+  }
+  // this range's partial result
+  float* my = part + ((((size_t)bi * sh.Hkv + kvh) * nsplit + split) * GL) * (D + 2);
+#pragma unroll
+  for (int g = 0; g < GL; ++g) {
+#pragma unroll
+    for (int i = 0; i < DPT; ++i) {
+      const int d = tid + 128 * i;
+      if (d < D) my[(size_t)g * (D + 2) + 2 + d] = o[g][i];
+    }
+    if (tid == 0) {
+      my[(size_t)g * (D + 2)] = m_s[g];
+      my[(size_t)g * (D + 2) + 1] = l_s[g];
     }
   }
   // the last CTA of this KV head merges the ranges in order
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     const int prev = atomicAdd(count + bi * sh.Hkv + kvh, 1);
     is_last = prev + 1 == nsplit;
   }
@@ -244,7 +311,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
   if (!is_last) return;
   __threadfence();
   const float* all = part + (((size_t)bi * sh.Hkv + kvh) * nsplit) * GL * (D + 2);
-  for (int i = threadIdx.x; i < G * sh.L * D; i += blockDim.x) {
+  for (int i = tid; i < G * sh.L * D; i += blockDim.x) {
     const int g = i / D, d = i % D;
     float mm = -INFINITY;
     for (int sp = 0; sp < nsplit; ++sp) mm = fmaxf(mm, __ldcg(all + ((size_t)sp * GL + g) * (D + 2)));
@@ -262,7 +329,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const float ob = __bfloat162float(__float2bfloat16_rn(oo / ll));
     out[(tok * sh.H + hq) * D + d] = __float2bfloat16_rn(ob * gate_sigmoid_bf16<NPT>(qkv + tok * sh.qkv_stride, hq, d));
   }
-  if (threadIdx.x == 0) count[bi * sh.Hkv + kvh] = 0;
+  if (tid == 0) count[bi * sh.Hkv + kvh] = 0;
+}
+
+template <int NPT, int GL>
+constexpr size_t attn_decode_smem() {
+  return (size_t)4 * kAttnTile * NPT * 32 * sizeof(__nv_bfloat16) + (size_t)GL * kAttnTile * sizeof(float);
 }
 
 // ---------------------------------------------------------------- prefill
@@ -411,7 +483,14 @@ extern "C" int qvx_attention(const void* qkv, long long qkv_stride, const void* 
     int* count = reinterpret_cast<int*>(static_cast<char*>(workspace) + ((pbytes + 255) & ~(size_t)255));
     const dim3 grid((unsigned)nsplit, (unsigned)Hkv, (unsigned)B);
 #define QVX_DEC(NPT_, GL_)                                                                                         \
-  attn_decode_kernel<NPT_, GL_><<<grid, kAttnWarps * 32, 0, s>>>(QB, QKV, KC, VC, OUT, part, count, pos_dev, pos, sh)
+  do {                                                                                                             \
+    constexpr size_t sm_ = attn_decode_smem<NPT_, GL_>();                                                          \
+    if (cudaFuncSetAttribute(attn_decode_kernel<NPT_, GL_>, cudaFuncAttributeMaxDynamicSharedMemorySize,           \
+                             (int)sm_) != cudaSuccess)                                                             \
+      return fail(QVX_ERR_CUDA, "qvx_attention: cannot raise the shared-memory limit");                            \
+    attn_decode_kernel<NPT_, GL_><<<grid, kAttnWarps * 32, sm_, s>>>(QB, QKV, KC, VC, OUT, part, count, pos_dev,   \
+                                                                      pos, sh);                                    \
+  } while (0)
     const int glp = GL <= 1 ? 1 : GL <= 2 ? 2 : GL <= 4 ? 4 : 8;
     if (D == 128) {
       if (glp == 1) QVX_DEC(4, 1); else if (glp == 2) QVX_DEC(4, 2); else if (glp == 4) QVX_DEC(4, 4); else QVX_DEC(4, 8);
