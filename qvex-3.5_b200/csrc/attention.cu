@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(128) attn_prep_kernel(const __nv_bfloat16* __r
                                                         const float* __restrict__ inv_freq, __nv_bfloat16* k_cache,
                                                         __nv_bfloat16* v_cache, __nv_bfloat16* __restrict__ q_out,
                                                         const int* pos_dev, int pos_host, AttnShape sh) {
+  pdl_grid_sync();
   constexpr int D = NPT * 32;
   const int lane = threadIdx.x & 31;
   const int slots = sh.H + 2 * sh.Hkv;
@@ -149,6 +150,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* k_cache,
     const __nv_bfloat16* v_cache, __nv_bfloat16* __restrict__ out, float* __restrict__ part, int* __restrict__ count,
     const int* pos_dev, int pos_host, AttnShape sh) {
+  pdl_grid_sync();
   constexpr int D = NPT * 32;
   constexpr int KT = kAttnTile;
   constexpr int DPT = D >= 128 ? D / 128 : 1;  // output features per thread
@@ -347,6 +349,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __nv_bfloat16* 
                                                            const __nv_bfloat16* k_cache, const __nv_bfloat16* v_cache,
                                                            __nv_bfloat16* __restrict__ out, const int* pos_dev,
                                                            int pos_host, AttnShape sh) {
+  pdl_grid_sync();
   constexpr int D = NPT * 32;
   constexpr int FP = D / 4;  // features per lane
   const int lane = threadIdx.x & 31;
@@ -465,9 +468,9 @@ extern "C" int qvx_attention(const void* qkv, long long qkv_stride, const void* 
   const long long pw = (long long)B * L * (H + 2 * Hkv);
   const unsigned pb = (unsigned)((pw + 3) / 4);
   switch (D) {
-    case 64: attn_prep_kernel<2><<<pb, 128, 0, s>>>(QKV, QN, KN, inv_freq, KC, VC, QB, pos_dev, pos, sh); break;
-    case 128: attn_prep_kernel<4><<<pb, 128, 0, s>>>(QKV, QN, KN, inv_freq, KC, VC, QB, pos_dev, pos, sh); break;
-    default: attn_prep_kernel<8><<<pb, 128, 0, s>>>(QKV, QN, KN, inv_freq, KC, VC, QB, pos_dev, pos, sh); break;
+    case 64: launch_pdl(attn_prep_kernel<2>, dim3(pb), dim3(128), 0, s, QKV, QN, KN, inv_freq, KC, VC, QB, pos_dev, pos, sh); break;
+    case 128: launch_pdl(attn_prep_kernel<4>, dim3(pb), dim3(128), 0, s, QKV, QN, KN, inv_freq, KC, VC, QB, pos_dev, pos, sh); break;
+    default: launch_pdl(attn_prep_kernel<8>, dim3(pb), dim3(128), 0, s, QKV, QN, KN, inv_freq, KC, VC, QB, pos_dev, pos, sh); break;
   }
   rc = check_launch("qvx_attention (prep)");
   if (rc) return rc;
@@ -488,7 +491,7 @@ extern "C" int qvx_attention(const void* qkv, long long qkv_stride, const void* 
     if (cudaFuncSetAttribute(attn_decode_kernel<NPT_, GL_>, cudaFuncAttributeMaxDynamicSharedMemorySize,           \
                              (int)sm_) != cudaSuccess)                                                             \
       return fail(QVX_ERR_CUDA, "qvx_attention: cannot raise the shared-memory limit");                            \
-    attn_decode_kernel<NPT_, GL_><<<grid, kAttnWarps * 32, sm_, s>>>(QB, QKV, KC, VC, OUT, part, count, pos_dev,   \
+    launch_pdl(attn_decode_kernel<NPT_, GL_>, dim3(grid), dim3(kAttnWarps * 32), sm_, s, QB, QKV, KC, VC, OUT, part, count, pos_dev,   \
                                                                       pos, sh);                                    \
   } while (0)
     const int glp = GL <= 1 ? 1 : GL <= 2 ? 2 : GL <= 4 ? 4 : 8;
@@ -505,9 +508,9 @@ extern "C" int qvx_attention(const void* qkv, long long qkv_stride, const void* 
   const long long aw = (long long)B * H * ((L + 7) / 8);
   const unsigned ab = (unsigned)((aw + 3) / 4);
   switch (D) {
-    case 64: attn_prefill_kernel<2><<<ab, 128, 0, s>>>(QB, QKV, KC, VC, OUT, pos_dev, pos, sh); break;
-    case 128: attn_prefill_kernel<4><<<ab, 128, 0, s>>>(QB, QKV, KC, VC, OUT, pos_dev, pos, sh); break;
-    default: attn_prefill_kernel<8><<<ab, 128, 0, s>>>(QB, QKV, KC, VC, OUT, pos_dev, pos, sh); break;
+    case 64: launch_pdl(attn_prefill_kernel<2>, dim3(ab), dim3(128), 0, s, QB, QKV, KC, VC, OUT, pos_dev, pos, sh); break;
+    case 128: launch_pdl(attn_prefill_kernel<4>, dim3(ab), dim3(128), 0, s, QB, QKV, KC, VC, OUT, pos_dev, pos, sh); break;
+    default: launch_pdl(attn_prefill_kernel<8>, dim3(ab), dim3(128), 0, s, QB, QKV, KC, VC, OUT, pos_dev, pos, sh); break;
   }
   return check_launch("qvx_attention (prefill)");
 }

@@ -8,6 +8,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <utility>
+
 #include "qvex.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -81,6 +83,33 @@ __device__ __forceinline__ uint32_t ld_nc_u16(const void* p) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// The small kernels of a decode step run under programmatic dependent launch: each CTA
+// first releases the dependent grid (so that a following projection kernel can start
+// streaming its weights while this one runs), then waits for the upstream grid before it
+// reads anything.  Every CTA does both before any early exit, so a grid's completion always
+// implies its upstream's, and the chain of waits stays transitive.
+__device__ __forceinline__ void pdl_grid_sync() {
+  pdl_launch_dependents();
+  pdl_wait();
+}
+
+// Launches `kern` with programmatic stream serialisation allowed (see pdl_grid_sync).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace qvx

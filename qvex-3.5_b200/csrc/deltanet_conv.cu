@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
     const __nv_bfloat16* state_in, __nv_bfloat16* state_out, __nv_bfloat16* state_mid, __nv_bfloat16* __restrict__ q,
     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v, __nv_bfloat16* __restrict__ a,
     __nv_bfloat16* __restrict__ b, int B, int T, int Hk, int Hv, float sc_q, float sc_k) {
+  pdl_grid_sync();
   constexpr int D = NPT * 32;
   constexpr int W = KW - 1;
   const int lane = threadIdx.x & 31;
@@ -155,7 +156,7 @@ extern "C" int qvx_deltanet_conv(const void* proj, long long proj_stride, const 
   auto aa = static_cast<__nv_bfloat16*>(a);
   auto bb = static_cast<__nv_bfloat16*>(b);
 #define QVX_CONV(NPT_)                                                                                           \
-  deltanet_conv_kernel<NPT_, 4><<<blocks, 128, 0, s>>>(P, proj_stride, conv_w, si, so, sm, qq, kk, vv, aa, bb, B, T, \
+  launch_pdl(deltanet_conv_kernel<NPT_, 4>, dim3(blocks), dim3(128), 0, s, P, proj_stride, conv_w, si, so, sm, qq, kk, vv, aa, bb, B, T, \
                                                       Hk, Hv, sc_q, sc_k)
   switch (Dk) {
     case 32: QVX_CONV(1); break;

@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(kGdWarps * 32) gated_delta_kernel(
     const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, const float* __restrict__ A_log,
     const float* __restrict__ dt_bias, const float* state_in, __nv_bfloat16* __restrict__ y, float* state_out,
     float* __restrict__ state_mid, int T, int Hk, int Hv, int Dv) {
+  pdl_grid_sync();
   constexpr int Dk = NPT * 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n = blockIdx.y;  // b * Hv + hv
@@ -218,13 +219,13 @@ extern "C" int qvx_gated_delta(const void* q, const void* k, const void* v, cons
   auto bb = static_cast<const __nv_bfloat16*>(b);
   auto yy = static_cast<__nv_bfloat16*>(y);
   if (Dk == 128)
-    gated_delta_kernel<4><<<grid, block, 0, s>>>(qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
+    launch_pdl(gated_delta_kernel<4>, dim3(grid), dim3(block), 0, s, qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
                                                  state_mid, T, Hk, Hv, Dv);
   else if (Dk == 64)
-    gated_delta_kernel<2><<<grid, block, 0, s>>>(qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
+    launch_pdl(gated_delta_kernel<2>, dim3(grid), dim3(block), 0, s, qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
                                                  state_mid, T, Hk, Hv, Dv);
   else
-    gated_delta_kernel<1><<<grid, block, 0, s>>>(qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
+    launch_pdl(gated_delta_kernel<1>, dim3(grid), dim3(block), 0, s, qq, kk, vv, aa, bb, A_log, dt_bias, state_in, yy, state_out,
                                                  state_mid, T, Hk, Hv, Dv);
   return check_launch("qvx_gated_delta");
 }

@@ -51,6 +51,7 @@ __device__ __forceinline__ float rbf16(float f) { return __bfloat162float(__floa
 __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* resid,
                                                         const __nv_bfloat16* __restrict__ w, float eps,
                                                         __nv_bfloat16* h_out, __nv_bfloat16* out, int D) {
+  pdl_grid_sync();
   __shared__ float warp_sum[32];
   const size_t row = blockIdx.x;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
@@ -99,6 +100,7 @@ __global__ void __launch_bounds__(256) gated_rms_norm_kernel(const __nv_bfloat16
                                                              const __nv_bfloat16* __restrict__ z, long long z_stride,
                                                              const __nv_bfloat16* __restrict__ w, float eps,
                                                              __nv_bfloat16* __restrict__ out, long long T, int H) {
+  pdl_grid_sync();
   constexpr int D = 32 * L;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long n = T * H * L;
@@ -131,6 +133,7 @@ __global__ void __launch_bounds__(256) gated_rms_norm_kernel(const __nv_bfloat16
 // out[m, i] = bf16(g * sigmoid(g) * u), g = gu[m, i], u = gu[m, I + i]; 8 outputs per thread.
 __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ gu, long long gu_stride,
                                                      __nv_bfloat16* __restrict__ out, long long M, long long I) {
+  pdl_grid_sync();
   const long long per_row = I / 8;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= M * per_row) return;
@@ -152,6 +155,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
 // engine/model.py:316 where no later kernel takes it over).
 __global__ void __launch_bounds__(256) add_kernel(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* out,
                                                   long long n8) {
+  pdl_grid_sync();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   const uint4 x = reinterpret_cast<const uint4*>(a)[i], y = reinterpret_cast<const uint4*>(b)[i];
@@ -174,7 +178,7 @@ extern "C" int qvx_add(const void* a, const void* b, void* out, long long n, voi
     return fail(QVX_ERR_ALIGN, "qvx_add: tensors need 16-byte alignment");
   if (n == 0) return QVX_OK;
   const long long n8 = n / 8;
-  add_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(add_kernel, dim3((unsigned)((n8 + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b), static_cast<__nv_bfloat16*>(out), n8);
   return check_launch("qvx_add");
 }
@@ -189,7 +193,7 @@ extern "C" int qvx_rms_norm(const void* x, const void* resid, const void* w, flo
       (h_out && !aligned(h_out, 16)))
     return fail(QVX_ERR_ALIGN, "qvx_rms_norm: tensors need 16-byte alignment");
   if (M == 0) return QVX_OK;
-  rms_norm_kernel<<<(unsigned)M, (D / 32 + 31) / 32 * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(rms_norm_kernel, dim3((unsigned)M), dim3((D / 32 + 31) / 32 * 32), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(resid),
       static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(h_out), static_cast<__nv_bfloat16*>(out),
       D);
@@ -214,11 +218,11 @@ extern "C" int qvx_gated_rms_norm(const void* y, const void* z, long long z_stri
   auto ww = static_cast<const __nv_bfloat16*>(w);
   auto oo = static_cast<__nv_bfloat16*>(out);
   switch (L) {
-    case 1: gated_rms_norm_kernel<1><<<blocks, 256, 0, s>>>(yy, zz, z_stride, ww, eps, oo, T, H); break;
-    case 2: gated_rms_norm_kernel<2><<<blocks, 256, 0, s>>>(yy, zz, z_stride, ww, eps, oo, T, H); break;
-    case 4: gated_rms_norm_kernel<4><<<blocks, 256, 0, s>>>(yy, zz, z_stride, ww, eps, oo, T, H); break;
-    case 8: gated_rms_norm_kernel<8><<<blocks, 256, 0, s>>>(yy, zz, z_stride, ww, eps, oo, T, H); break;
-    default: gated_rms_norm_kernel<16><<<blocks, 256, 0, s>>>(yy, zz, z_stride, ww, eps, oo, T, H); break;
+    case 1: launch_pdl(gated_rms_norm_kernel<1>, dim3(blocks), dim3(256), 0, s, yy, zz, z_stride, ww, eps, oo, T, H); break;
+    case 2: launch_pdl(gated_rms_norm_kernel<2>, dim3(blocks), dim3(256), 0, s, yy, zz, z_stride, ww, eps, oo, T, H); break;
+    case 4: launch_pdl(gated_rms_norm_kernel<4>, dim3(blocks), dim3(256), 0, s, yy, zz, z_stride, ww, eps, oo, T, H); break;
+    case 8: launch_pdl(gated_rms_norm_kernel<8>, dim3(blocks), dim3(256), 0, s, yy, zz, z_stride, ww, eps, oo, T, H); break;
+    default: launch_pdl(gated_rms_norm_kernel<16>, dim3(blocks), dim3(256), 0, s, yy, zz, z_stride, ww, eps, oo, T, H); break;
   }
   return check_launch("qvx_gated_rms_norm");
 }
@@ -232,7 +236,7 @@ extern "C" int qvx_swiglu(const void* gu, long long gu_stride, void* out, long l
   if (!aligned(gu, 16) || !aligned(out, 16)) return fail(QVX_ERR_ALIGN, "qvx_swiglu: tensors need 16-byte alignment");
   if (M == 0) return QVX_OK;
   const long long n = M * (I / 8);
-  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(gu), gu_stride, static_cast<__nv_bfloat16*>(out), M, I);
   return check_launch("qvx_swiglu");
 }

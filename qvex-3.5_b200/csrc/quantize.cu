@@ -311,6 +311,7 @@ __global__ void __launch_bounds__(256) dequantize_rows_kernel(const uint32_t* __
                                                               const int32_t* __restrict__ ids, int n_ids,
                                                               uint4* __restrict__ out, int N, int KW,
                                                               int* __restrict__ status) {
+  pdl_grid_sync();
   const long long total = (long long)n_ids * KW;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -397,7 +398,7 @@ extern "C" int qvx_dequantize_rows(const uint32_t* wq, const void* scales, const
   int* status = device_status_ptr();
   if (!status) return fail(QVX_ERR_CUDA, "qvx_dequantize_rows: device status word unavailable");
   const long long work = (long long)n_ids * (K / 8);
-  dequantize_rows_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(dequantize_rows_kernel, dim3(grid_for(work, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), 
       wq, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases), ids, n_ids,
       static_cast<uint4*>(out), N, K / 8, status);
   return check_launch("qvx_dequantize_rows");

@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1)
     sample_scores_kernel(const void* __restrict__ logits, int bf16, const float* __restrict__ seen,
                          float* __restrict__ scores, int V, float temperature, float top_p, int top_k,
                          float presence_penalty) {
+  pdl_grid_sync();
   __shared__ SmpShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
   const size_t row = blockIdx.x;
@@ -270,6 +271,7 @@ __global__ void __cluster_dims__(kSmpCluster, 1, 1) __launch_bounds__(kSmpThread
     sample_scores_cluster_kernel(const void* __restrict__ logits, int bf16, const float* __restrict__ seen,
                                  float* __restrict__ scores, int V, float temperature, float top_p, int top_k,
                                  float presence_penalty) {
+  pdl_grid_sync();
   __shared__ SmpClusterShared sh;
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
@@ -408,6 +410,7 @@ __device__ __forceinline__ void better(float& best, int& idx, float v, int i) {
 __global__ void __cluster_dims__(kSmpCluster, 1, 1) __launch_bounds__(kSmpThreads, 1)
     sample_pick_kernel(const float* __restrict__ scores, int32_t* __restrict__ tokens, int V, int greedy,
                        unsigned long long seed, unsigned long long offset) {
+  pdl_grid_sync();
   __shared__ SmpPickShared sh;
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
@@ -485,10 +488,10 @@ extern "C" int qvx_sample_scores(const void* logits, int logits_dtype, const flo
   const int k = (top_k > 0 && top_k < V) ? top_k : 0;
   const long long per_thread = ((long long)(V + kSmpCluster - 1) / kSmpCluster + kSmpThreads - 1) / kSmpThreads;
   if ((long long)k * per_thread <= kSmpCandCap && k <= kSmpCandCap / kSmpCluster) {
-    sample_scores_cluster_kernel<<<M * kSmpCluster, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+    launch_pdl(sample_scores_cluster_kernel, dim3(M * kSmpCluster), dim3(kSmpThreads), 0, static_cast<cudaStream_t>(stream), 
         logits, logits_dtype == 0, seen, scores, V, temperature, top_p, top_k, presence_penalty);
   } else {
-    sample_scores_kernel<<<M, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+    launch_pdl(sample_scores_kernel, dim3(M), dim3(kSmpThreads), 0, static_cast<cudaStream_t>(stream), 
         logits, logits_dtype == 0, seen, scores, V, temperature, top_p, top_k, presence_penalty);
   }
   return check_launch("qvx_sample_scores");
@@ -501,7 +504,7 @@ extern "C" int qvx_sample_pick(const float* scores, int32_t* tokens, int M, int 
   if (M == 0) return QVX_OK;
   if (!scores || !tokens) return fail(QVX_ERR_INVALID, "qvx_sample_pick: null pointer");
   if (!aligned(scores, 4) || !aligned(tokens, 4)) return fail(QVX_ERR_ALIGN, "qvx_sample_pick: misaligned buffer");
-  sample_pick_kernel<<<M * kSmpCluster, kSmpThreads, 0, static_cast<cudaStream_t>(stream)>>>(scores, tokens, V,
+  launch_pdl(sample_pick_kernel, dim3(M * kSmpCluster), dim3(kSmpThreads), 0, static_cast<cudaStream_t>(stream), scores, tokens, V,
                                                                                               greedy, seed, offset);
   return check_launch("qvx_sample_pick");
 }
