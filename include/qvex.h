@@ -326,7 +326,7 @@ size_t qvx_attention_workspace_size(int B, int Hkv, int G, int L, int D, int nsp
  *   out       bf16 [B, L, H*D] = sdpa(q, k, v, scale, causal) * sigmoid(gate)
  * The position is *pos_dev when pos_dev is non-NULL (a device int32, so that one CUDA graph
  * serves every step), else pos.  With a workspace of qvx_attention_workspace_size(...)
- * bytes (256-byte aligned) and G * L <= 8 the keys are split over nsplit CTAs per KV head
+ * bytes (256-byte aligned) and G * L <= 8 the keys are split over nsplit (1..64) CTAs per KV head
  * (decode); otherwise one warp serves eight queries of a head (prefill).  D in {64, 128,
  * 256}; rotary_dim a multiple of 2*D/32, <= D. */
 int qvx_attention(const void* qkv, long long qkv_stride, const void* q_norm, const void* k_norm, float eps,

@@ -312,23 +312,46 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  // merge: every range's (max, sum) into shared memory at once, the weights
+  // f = exp(m_range - m_max) per (range, query), then the outputs as independent loads
   const float* all = part + (((size_t)bi * sh.Hkv + kvh) * nsplit) * GL * (D + 2);
+  float* fm = reinterpret_cast<float*>(Ks);  // [nsplit][GL] range maxima, then weights
+  float* fl = fm + nsplit * GL;              // [nsplit][GL] range sums
+  float* mx_s = fl + nsplit * GL;            // [GL] maxima, then totals
+  for (int i = tid; i < nsplit * GL; i += blockDim.x) {
+    const float* pp = all + (size_t)i * (D + 2);
+    fm[i] = __ldcg(pp);
+    fl[i] = __ldcg(pp + 1);
+  }
+  __syncthreads();
+  if (tid < GL) {
+    float mm = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) mm = fmaxf(mm, fm[sp * GL + tid]);
+    mx_s[tid] = mm;
+  }
+  __syncthreads();
+  for (int i = tid; i < nsplit * GL; i += blockDim.x) {
+    const float ms = fm[i];
+    fm[i] = ms == -INFINITY ? 0.0f : expf(ms - mx_s[i % GL]);
+  }
+  __syncthreads();
+  if (tid < GL) {
+    float ll = 0.0f;
+    for (int sp = 0; sp < nsplit; ++sp) ll = fmaf(fl[sp * GL + tid], fm[sp * GL + tid], ll);
+    mx_s[tid] = ll;
+  }
+  __syncthreads();
   for (int i = tid; i < G * sh.L * D; i += blockDim.x) {
     const int g = i / D, d = i % D;
-    float mm = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) mm = fmaxf(mm, __ldcg(all + ((size_t)sp * GL + g) * (D + 2)));
-    float ll = 0.0f, oo = 0.0f;
+    float oo = 0.0f;
+#pragma unroll 8
     for (int sp = 0; sp < nsplit; ++sp) {
-      const float* pp = all + ((size_t)sp * GL + g) * (D + 2);
-      const float ms = __ldcg(pp);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - mm);
-      ll = fmaf(__ldcg(pp + 1), f, ll);
-      oo = fmaf(__ldcg(pp + 2 + d), f, oo);
+      const float f = fm[sp * GL + g];
+      if (f != 0.0f) oo = fmaf(__ldcg(all + ((size_t)sp * GL + g) * (D + 2) + 2 + d), f, oo);
     }
     const int t = g / G, hq = kvh * G + g % G;
     const size_t tok = (size_t)bi * sh.L + t;
-    const float ob = __bfloat162float(__float2bfloat16_rn(oo / ll));
+    const float ob = __bfloat162float(__float2bfloat16_rn(oo / mx_s[g]));
     out[(tok * sh.H + hq) * D + d] = __float2bfloat16_rn(ob * gate_sigmoid_bf16<NPT>(qkv + tok * sh.qkv_stride, hq, d));
   }
   if (tid == 0) count[bi * sh.Hkv + kvh] = 0;
@@ -477,8 +500,8 @@ extern "C" int qvx_attention(const void* qkv, long long qkv_stride, const void* 
   const int G = H / Hkv;
   const int GL = G * L;
   if (workspace && GL <= kAttnMaxQ) {
-    if (nsplit < 1 || workspace_bytes < qvx_attention_workspace_size(B, Hkv, G, L, D, nsplit))
-      return fail(QVX_ERR_WORKSPACE, "qvx_attention: workspace of %zu bytes, %zu needed for %d splits",
+    if (nsplit < 1 || nsplit > 64 || workspace_bytes < qvx_attention_workspace_size(B, Hkv, G, L, D, nsplit))
+      return fail(QVX_ERR_WORKSPACE, "qvx_attention: workspace of %zu bytes, %zu needed for %d splits (1..64)",
                   workspace_bytes, qvx_attention_workspace_size(B, Hkv, G, L, D, nsplit), nsplit);
     if (!aligned(workspace, 256)) return fail(QVX_ERR_ALIGN, "qvx_attention: workspace needs 256-byte alignment");
     float* part = static_cast<float*>(workspace);

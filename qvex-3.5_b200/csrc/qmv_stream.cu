@@ -280,11 +280,9 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     const int k0 = wt * 1024 + lane * 32;
     const bool kact = FULLK || k0 < K;
     const int g = kact ? (k0 >> 6) : 0;
-    pdl_wait();  // x comes from the upstream kernel
     auto xrow = [&](int m) { return x + (size_t)(m0 + m) * io.x_stride; };
-    // a lane's 32 inputs of token m as 16 packed bf16 pairs (zeros when out of range)
-    auto load_raw = [&](int m, bool live, uint32_t (&u)[16]) {
-      const uint4* src = reinterpret_cast<const uint4*>(xrow(live ? m : 0) + (live ? k0 : 0));
+    auto ld16 = [&](const __nv_bfloat16* p, bool live, uint32_t (&u)[16]) {
+      const uint4* src = reinterpret_cast<const uint4*>(p);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint4 t = live ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
@@ -301,14 +299,29 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       }
       return ss;
     };
+    // the norm weights do not come from the upstream kernel: in flight before the wait
+    uint32_t wn[16];
+    const bool has_w = io.in_mode == kInRmsNorm || io.in_mode == kInGatedRms;
+    ld16(io.in_mode == kInRmsNorm ? io.norm_w + (kact ? k0 : 0) : io.norm_w + (lane % max(io.head_lanes, 1)) * 32,
+         has_w && kact, wn);
+    pdl_wait();  // x (and z, the gate|up rows, the residual) come from upstream kernels
+    // every token's inputs (and the second operand of SwiGLU / the gated norm) in one round trip
+    uint32_t u[MC][16], aux[MC][16];
+#pragma unroll
+    for (int m = 0; m < MC; ++m) {
+      const bool live = kact && m < mc;
+      ld16(xrow(live ? m : 0) + (live ? k0 : 0), live, u[m]);
+      const bool has_aux = io.in_mode == kInSwiglu || io.in_mode == kInGatedRms;
+      ld16(io.in_mode == kInSwiglu ? xrow(live ? m : 0) + K + (live ? k0 : 0)
+                                   : io.z + (size_t)(m0 + (live ? m : 0)) * io.z_stride + (live ? k0 : 0),
+           has_aux && live, aux[m]);
+    }
     if (io.in_mode == kInRmsNorm) {
       // the row's sum of squares: a lane's 32 inputs in order, a butterfly over the warp,
       // then the warps of the team in order (qvx_rms_norm's order)
 #pragma unroll
       for (int m = 0; m < MC; ++m) {
-        uint32_t u[16];
-        load_raw(m, kact && m < mc, u);
-        float ss = sumsq(u);
+        float ss = sumsq(u[m]);
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) row_ss[m * CW + warp] = ss;
@@ -319,56 +332,40 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
 #pragma unroll
     for (int m = 0; m < MC; ++m) {
       const bool live = kact && m < mc;
-      uint32_t u[16];
-      load_raw(m, live, u);
       if (io.in_mode != kInPlain) {
-        // the transform in chunks of 8 inputs (one 16-byte piece of every operand at a time)
         float r = 0.0f;
         if (io.in_mode == kInRmsNorm) {
           float tot = row_ss[m * CW + team * P];
           for (int p = 1; p < P; ++p) tot += row_ss[m * CW + team * P + p];
           r = 1.0f / sqrtf(tot / (float)K + io.eps);
         } else if (io.in_mode == kInGatedRms) {
-          float ss = sumsq(u);
+          float ss = sumsq(u[m]);
           for (int o = io.head_lanes / 2; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
           r = 1.0f / sqrtf(ss / (float)(32 * io.head_lanes) + io.eps);
         }
         if (live) {
-          const uint4* aux = io.in_mode == kInRmsNorm ? reinterpret_cast<const uint4*>(io.norm_w + k0)
-                             : io.in_mode == kInSwiglu ? reinterpret_cast<const uint4*>(xrow(m) + K + k0)
-                                                       : reinterpret_cast<const uint4*>(io.z + (size_t)(m0 + m) * io.z_stride + k0);
-          const uint4* wn = reinterpret_cast<const uint4*>(io.norm_w + (lane % max(io.head_lanes, 1)) * 32);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 a4 = __ldg(aux + c);
-            const uint32_t av[4] = {a4.x, a4.y, a4.z, a4.w};
-            uint4 w4 = make_uint4(0, 0, 0, 0);
-            if (io.in_mode == kInGatedRms) w4 = __ldg(wn + c);
-            const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          for (int j = 0; j < 16; ++j) {
+            float v2[2];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float v2[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const uint32_t xs = h ? (u[4 * c + j] & 0xffff0000u) : (u[4 * c + j] << 16);
-                const uint32_t as = h ? (av[j] & 0xffff0000u) : (av[j] << 16);
-                const float xv = __uint_as_float(xs), aa = __uint_as_float(as);
-                if (io.in_mode == kInRmsNorm) {
-                  v2[h] = aa * rbf(xv * r);
-                } else if (io.in_mode == kInSwiglu) {
-                  v2[h] = xv * (1.0f / (1.0f + expf(-xv))) * aa;
-                } else {
-                  const float ww = __uint_as_float(h ? (wv[j] & 0xffff0000u) : (wv[j] << 16));
-                  const float nrm = rbf(ww * rbf(xv * r));
-                  v2[h] = aa * (1.0f / (1.0f + expf(-aa))) * nrm;
-                }
+            for (int h = 0; h < 2; ++h) {
+              const float xv = __uint_as_float(h ? (u[m][j] & 0xffff0000u) : (u[m][j] << 16));
+              const float aa = __uint_as_float(h ? (aux[m][j] & 0xffff0000u) : (aux[m][j] << 16));
+              const float ww = __uint_as_float(h ? (wn[j] & 0xffff0000u) : (wn[j] << 16));
+              if (io.in_mode == kInRmsNorm) {
+                v2[h] = ww * rbf(xv * r);
+              } else if (io.in_mode == kInSwiglu) {
+                v2[h] = xv * (1.0f / (1.0f + expf(-xv))) * aa;
+              } else {
+                const float nrm = rbf(ww * rbf(xv * r));
+                v2[h] = aa * (1.0f / (1.0f + expf(-aa))) * nrm;
               }
-              u[4 * c + j] = bf16x2_bits(v2[0], v2[1]);
             }
+            u[m][j] = bf16x2_bits(v2[0], v2[1]);
           }
         }
       }
-      make_planes<PL>(u, xp[m]);
+      make_planes<PL>(u[m], xp[m]);
     }
     for (int c = 0; c < nchunks; ++c) {
       const int s_ = c % S;
@@ -444,14 +441,27 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
   } else {
     // ------------------------------------------------------------ reducer
     if (io.resid) pdl_wait();  // the residual comes from the upstream kernel
+    constexpr int kResPer = (4 * 8 * MC + 31) / 32;  // residual values per lane per stage (R * MC <= 32 MC)
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % S;
       const uint32_t ph = (uint32_t)(c / S) & 1u;
-      if (!mbar_wait(&done[s], ph, abort_flag, status)) break;
       const int r0 = chunk_row(c);
       const int nr = min(R, r_end - r0);
+      // the stage's residual values, loaded while the compute warps still work on it
+      float resv[kResPer];
+      if (io.resid && !(gather && g.mode == kExReduce)) {
+#pragma unroll
+        for (int i = 0; i < kResPer; ++i) {
+          const int v = lane + 32 * i, r = v / MC, m = v % MC;
+          resv[i] = (v < R * MC && r < nr && m < mc) ? __bfloat162float(io.resid[(size_t)(m0 + m) * N + r0 + r]) : 0.0f;
+        }
+      }
+      if (!mbar_wait(&done[s], ph, abort_flag, status)) break;
       const float* red = reinterpret_cast<const float*>(stage(s) + (size_t)R * K / 2 + (size_t)R * K / 16);
-      for (int v = lane; v < R * MC; v += 32) {
+#pragma unroll
+      for (int i = 0; i < kResPer; ++i) {
+        const int v = lane + 32 * i;
+        if (v >= R * MC) break;
         const int r = v / MC, m = v % MC;
         const int team = r / RT, idx = (r % RT) * MC + m;
         if (r < nr && m < mc) {
@@ -462,8 +472,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
             reinterpret_cast<float*>(g.out[g.rank])[(size_t)(m0 + m) * N + r0 + r] = acc;
           } else {
             __nv_bfloat16 yv = __float2bfloat16_rn(acc);
-            if (io.resid)
-              yv = __float2bfloat16_rn(__bfloat162float(io.resid[(size_t)(m0 + m) * N + r0 + r]) + __bfloat162float(yv));
+            if (io.resid) yv = __float2bfloat16_rn(resv[i] + __bfloat162float(yv));
             if (gather) {
               // this rank's own full output; the peers get the CTA's rows once, at the end
               // (a peer store here would make every stage release wait for NVLink)
