@@ -56,11 +56,11 @@ __global__ void __launch_bounds__(128) attn_prep_kernel(const __nv_bfloat16* __r
   const __nv_bfloat16* src = kind == 0 ? row + (size_t)slot * 2 * D : row + (size_t)sh.H * 2 * D + (size_t)(slot - sh.H) * D;
   float x[NPT];
 #pragma unroll
-  for (int i = 0; i < NPT; ++i) x[i] = __bfloat162float(src[lane * NPT + i]);
+  for (int i = 0; i < NPT; ++i) x[i] = __bfloat162float(__ldcg(src + lane * NPT + i));
   if (kind == 2) {
     __nv_bfloat16* dst = v_cache + (((size_t)bi * sh.Hkv + (slot - sh.H - sh.Hkv)) * sh.cap + p) * D + lane * NPT;
 #pragma unroll
-    for (int i = 0; i < NPT; ++i) dst[i] = src[lane * NPT + i];
+    for (int i = 0; i < NPT; ++i) dst[i] = __ldcg(src + lane * NPT + i);
     return;
   }
   float ss = 0.0f;
@@ -107,7 +107,7 @@ constexpr int kAttnTile = 64;   // keys per shared-memory tile
 template <int NPT>
 __device__ __forceinline__ float gate_sigmoid_bf16(const __nv_bfloat16* row, int h, int d) {
   constexpr int D = NPT * 32;
-  const float g = __bfloat162float(row[(size_t)h * 2 * D + D + d]);
+  const float g = __bfloat162float(__ldcg(row + (size_t)h * 2 * D + D + d));
   return __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-g))));
 }
 
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(
     const bool live = g < G * sh.L;
 #pragma unroll
     for (int i = 0; i < NPT; ++i)
-      qv[g][i] = live ? __bfloat162float(q[(((size_t)bi * sh.L + t) * sh.H + hq) * D + lane * NPT + i]) : 0.0f;
+      qv[g][i] = live ? __bfloat162float(__ldcg(q + (((size_t)bi * sh.L + t) * sh.H + hq) * D + lane * NPT + i)) : 0.0f;
   }
   if (tid < GL) {
     m_s[tid] = -INFINITY;
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __nv_bfloat16* 
   const __nv_bfloat16* qr = q + (((size_t)bi * sh.L + tt) * sh.H + h) * D + part * FP;
 #pragma unroll
   for (int i = 0; i < FP; ++i) {
-    qv[i] = __bfloat162float(qr[i]);
+    qv[i] = __bfloat162float(__ldcg(qr + i));
     o[i] = 0.0f;
   }
   float m = -INFINITY, l = 0.0f;
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __nv_bfloat16* 
     float s = 0.0f;
 #pragma unroll
     for (int c = 0; c < FP / 8; ++c) {
-      const uint4 kv = __ldg(kr + c);
+      const uint4 kv = __ldcg(kr + c);
       const uint32_t u[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __nv_bfloat16* 
     const uint4* vr = reinterpret_cast<const uint4*>(vc + (size_t)j * D);
 #pragma unroll
     for (int c = 0; c < FP / 8; ++c) {
-      const uint4 vv = __ldg(vr + c);
+      const uint4 vv = __ldcg(vr + c);
       const uint32_t u[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {

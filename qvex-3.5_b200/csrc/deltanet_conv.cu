@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
     const __nv_bfloat16* src = r < W ? state_in + ((size_t)bi * W + r) * C + ch0
                                      : proj + ((size_t)bi * T + (r - W)) * proj_stride + ch0;
 #pragma unroll
-    for (int i = 0; i < NPT; ++i) out[i] = __bfloat162float(src[i]);
+    for (int i = 0; i < NPT; ++i) out[i] = __bfloat162float(__ldcg(src + i));
   };
   float win[W][NPT];
 #pragma unroll
@@ -113,8 +113,8 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
       for (int i = 0; i < NPT; ++i) dst[i] = __float2bfloat16_rn(s[i]);
       if (lane == 0) {
         const __nv_bfloat16* pr = proj + row * proj_stride + C + value_dim;
-        b[row * Hv + h] = pr[h];
-        a[row * Hv + h] = pr[Hv + h];
+        b[row * Hv + h] = __ldcg(pr + h);
+        a[row * Hv + h] = __ldcg(pr + Hv + h);
       }
     }
   }

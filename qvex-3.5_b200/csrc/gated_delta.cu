@@ -51,14 +51,14 @@ __device__ __forceinline__ void reduce4_all(float (&p)[4], int lane) {
 template <int NPT>
 __device__ __forceinline__ void load_bf16_vec(const __nv_bfloat16* p, float (&out)[NPT]) {
   if constexpr (NPT == 4) {
-    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    const uint2 t = __ldcg(reinterpret_cast<const uint2*>(p));
     out[0] = __uint_as_float(t.x << 16); out[1] = __uint_as_float(t.x & 0xffff0000u);
     out[2] = __uint_as_float(t.y << 16); out[3] = __uint_as_float(t.y & 0xffff0000u);
   } else if constexpr (NPT == 2) {
-    const uint32_t t = *reinterpret_cast<const uint32_t*>(p);
+    const uint32_t t = __ldcg(reinterpret_cast<const unsigned int*>(p));
     out[0] = __uint_as_float(t << 16); out[1] = __uint_as_float(t & 0xffff0000u);
   } else {
-    out[0] = __bfloat162float(*p);
+    out[0] = __bfloat162float(__ldcg(p));
   }
 }
 
@@ -75,11 +75,11 @@ __device__ __forceinline__ void gd_load_step(GdStep& s, const __nv_bfloat16* qp,
   load_bf16_vec<NPT>(kp, tk);
 #pragma unroll
   for (int i = 0; i < NPT; ++i) { s.q[i] = tq[i]; s.k[i] = tk[i]; }
-  const uint2 tv = *reinterpret_cast<const uint2*>(vp);  // 4 consecutive bf16 rows
+  const uint2 tv = __ldcg(reinterpret_cast<const uint2*>(vp));  // 4 consecutive bf16 rows
   s.v[0] = __uint_as_float(tv.x << 16); s.v[1] = __uint_as_float(tv.x & 0xffff0000u);
   s.v[2] = __uint_as_float(tv.y << 16); s.v[3] = __uint_as_float(tv.y & 0xffff0000u);
-  s.a = __bfloat162float(*ap);
-  s.b = __bfloat162float(*bp);
+  s.a = __bfloat162float(__ldcg(ap));
+  s.b = __bfloat162float(__ldcg(bp));
 }
 
 // A lane's NPT consecutive state floats as one 16-, 8- or 4-byte access (state pointers are
@@ -87,13 +87,13 @@ __device__ __forceinline__ void gd_load_step(GdStep& s, const __nv_bfloat16* qp,
 template <int NPT>
 __device__ __forceinline__ void ld_state(const float* p, float (&v)[NPT]) {
   if constexpr (NPT == 4) {
-    const float4 t = *reinterpret_cast<const float4*>(p);
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(p));
     v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
   } else if constexpr (NPT == 2) {
-    const float2 t = *reinterpret_cast<const float2*>(p);
+    const float2 t = __ldcg(reinterpret_cast<const float2*>(p));
     v[0] = t.x; v[1] = t.y;
   } else {
-    v[0] = *p;
+    v[0] = __ldcg(p);
   }
 }
 template <int NPT>

@@ -15,11 +15,15 @@
 
 namespace qvx {
 
-__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float (&v)[32]) {
+// 32 consecutive bf16 values.  Tensors written by an upstream kernel are read at L2
+// (ld.global.cg): these kernels run under programmatic dependent launch, so a CTA may start
+// while the upstream grid still writes, and neither the read-only path nor a line left in the
+// SM's L1 may serve such data.  Constant parameters (norm weights) take the read-only path.
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float (&v)[32], bool upstream = true) {
   const uint4* q = reinterpret_cast<const uint4*>(p);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const uint4 t = q[c];
+    const uint4 t = upstream ? __ldcg(q + c) : __ldg(q + c);
     const uint32_t u[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -83,7 +87,7 @@ __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16* x, 
   if (!live) return;
   if (w) {
     float wv[32];
-    load_bf16x32(w + 32 * t, wv);
+    load_bf16x32(w + 32 * t, wv, false);
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = wv[i] * rbf16(v[i] * r);
   } else {
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(256) gated_rms_norm_kernel(const __nv_bfloat16
   const float r = 1.0f / sqrtf(s / (float)D + eps);
   float zv[32], wv[32];
   load_bf16x32(z + t * z_stride + (long long)h * D + 32 * part, zv);
-  load_bf16x32(w + 32 * part, wv);
+  load_bf16x32(w + 32 * part, wv, false);
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const float nrm = rbf16(wv[i] * rbf16(v[i] * r));
@@ -138,8 +142,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= M * per_row) return;
   const long long m = gid / per_row, c = (gid % per_row) * 8;
-  const uint4 gv = *reinterpret_cast<const uint4*>(gu + m * gu_stride + c);
-  const uint4 uv = *reinterpret_cast<const uint4*>(gu + m * gu_stride + I + c);
+  const uint4 gv = __ldcg(reinterpret_cast<const uint4*>(gu + m * gu_stride + c));
+  const uint4 uv = __ldcg(reinterpret_cast<const uint4*>(gu + m * gu_stride + I + c));
   const uint32_t ga[4] = {gv.x, gv.y, gv.z, gv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
   uint32_t o[4];
 #pragma unroll
@@ -158,7 +162,7 @@ __global__ void __launch_bounds__(256) add_kernel(const __nv_bfloat16* a, const 
   pdl_grid_sync();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n8) return;
-  const uint4 x = reinterpret_cast<const uint4*>(a)[i], y = reinterpret_cast<const uint4*>(b)[i];
+  const uint4 x = __ldcg(reinterpret_cast<const uint4*>(a) + i), y = __ldcg(reinterpret_cast<const uint4*>(b) + i);
   const uint32_t xa[4] = {x.x, x.y, x.z, x.w}, ya[4] = {y.x, y.y, y.z, y.w};
   uint32_t o[4];
 #pragma unroll

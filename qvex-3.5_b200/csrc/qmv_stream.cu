@@ -281,11 +281,15 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     const bool kact = FULLK || k0 < K;
     const int g = kact ? (k0 >> 6) : 0;
     auto xrow = [&](int m) { return x + (size_t)(m0 + m) * io.x_stride; };
-    auto ld16 = [&](const __nv_bfloat16* p, bool live, uint32_t (&u)[16]) {
+    // Operands written by upstream kernels (x, z, the gate|up rows) are read at L2
+    // (ld.global.cg): under programmatic dependent launch this CTA may start while the
+    // upstream grid still writes them, so neither the read-only path nor a line left in this
+    // SM's L1 may serve them.  Constant parameters (norm weights) take the read-only path.
+    auto ld16 = [&](const __nv_bfloat16* p, bool live, uint32_t (&u)[16], bool upstream) {
       const uint4* src = reinterpret_cast<const uint4*>(p);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const uint4 t = live ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+        const uint4 t = !live ? make_uint4(0, 0, 0, 0) : upstream ? __ldcg(src + c) : __ldg(src + c);
         u[4 * c] = t.x; u[4 * c + 1] = t.y; u[4 * c + 2] = t.z; u[4 * c + 3] = t.w;
       }
     };
@@ -303,18 +307,18 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     uint32_t wn[16];
     const bool has_w = io.in_mode == kInRmsNorm || io.in_mode == kInGatedRms;
     ld16(io.in_mode == kInRmsNorm ? io.norm_w + (kact ? k0 : 0) : io.norm_w + (lane % max(io.head_lanes, 1)) * 32,
-         has_w && kact, wn);
+         has_w && kact, wn, false);
     pdl_wait();  // x (and z, the gate|up rows, the residual) come from upstream kernels
     // every token's inputs (and the second operand of SwiGLU / the gated norm) in one round trip
     uint32_t u[MC][16], aux[MC][16];
 #pragma unroll
     for (int m = 0; m < MC; ++m) {
       const bool live = kact && m < mc;
-      ld16(xrow(live ? m : 0) + (live ? k0 : 0), live, u[m]);
+      ld16(xrow(live ? m : 0) + (live ? k0 : 0), live, u[m], true);
       const bool has_aux = io.in_mode == kInSwiglu || io.in_mode == kInGatedRms;
       ld16(io.in_mode == kInSwiglu ? xrow(live ? m : 0) + K + (live ? k0 : 0)
                                    : io.z + (size_t)(m0 + (live ? m : 0)) * io.z_stride + (live ? k0 : 0),
-           has_aux && live, aux[m]);
+           has_aux && live, aux[m], true);
     }
     if (io.in_mode == kInRmsNorm) {
       // the row's sum of squares: a lane's 32 inputs in order, a butterfly over the warp,
@@ -453,7 +457,8 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
 #pragma unroll
         for (int i = 0; i < kResPer; ++i) {
           const int v = lane + 32 * i, r = v / MC, m = v % MC;
-          resv[i] = (v < R * MC && r < nr && m < mc) ? __bfloat162float(io.resid[(size_t)(m0 + m) * N + r0 + r]) : 0.0f;
+          resv[i] = (v < R * MC && r < nr && m < mc) ? __bfloat162float(__ldcg(io.resid + (size_t)(m0 + m) * N + r0 + r))
+                                                      : 0.0f;
         }
       }
       if (!mbar_wait(&done[s], ph, abort_flag, status)) break;
@@ -546,7 +551,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
             }
             if (late) break;
             __nv_bfloat16 yv = __float2bfloat16_rn(tot);
-            if (io.resid) yv = __float2bfloat16_rn(__bfloat162float(io.resid[e]) + __bfloat162float(yv));
+            if (io.resid) yv = __float2bfloat16_rn(__bfloat162float(__ldcg(io.resid + e)) + __bfloat162float(yv));
             y[e] = yv;
           }
       } else {

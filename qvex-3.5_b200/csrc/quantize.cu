@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(256) dequantize_rows_kernel(const uint32_t* __
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int r = (int)(i / KW), j = (int)(i % KW);
-    const int id = ids[r];
+    const int id = __ldcg(ids + r);
     if (id < 0 || id >= N) {
       out[i] = make_uint4(0, 0, 0, 0);
       if (j == 0) set_device_status(status, QVX_ERR_INVALID);

@@ -120,9 +120,9 @@ __global__ void __launch_bounds__(kSmpThreads, 1)
   // 1. penalised, tempered logits
   float mx = -INFINITY;
   for (int i = tid; i < V; i += kSmpThreads) {
-    float v = bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(logits)[row * (size_t)V + i])
-                   : static_cast<const float*>(logits)[row * (size_t)V + i];
-    if (penal) v = __fsub_rn(v, __fmul_rn(presence_penalty, seen[i]));
+    float v = bf16 ? __bfloat162float(__ldcg(static_cast<const __nv_bfloat16*>(logits) + row * (size_t)V + i))
+                   : __ldcg(static_cast<const float*>(logits) + row * (size_t)V + i);
+    if (penal) v = __fsub_rn(v, __fmul_rn(presence_penalty, __ldcg(seen + i)));
     if (!greedy) v = __fdiv_rn(v, temperature);
     l[i] = v;
     mx = fmaxf(mx, v);
@@ -287,9 +287,9 @@ __global__ void __cluster_dims__(kSmpCluster, 1, 1) __launch_bounds__(kSmpThread
   // 1. penalised, tempered logits; each thread's maximum
   float mt = -INFINITY;
   for (int i = e0 + tid; i < e1; i += kSmpThreads) {
-    float v = bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(logits)[row * (size_t)V + i])
-                   : static_cast<const float*>(logits)[row * (size_t)V + i];
-    if (penal) v = __fsub_rn(v, __fmul_rn(presence_penalty, seen[i]));
+    float v = bf16 ? __bfloat162float(__ldcg(static_cast<const __nv_bfloat16*>(logits) + row * (size_t)V + i))
+                   : __ldcg(static_cast<const float*>(logits) + row * (size_t)V + i);
+    if (penal) v = __fsub_rn(v, __fmul_rn(presence_penalty, __ldcg(seen + i)));
     if (!greedy) v = __fdiv_rn(v, temperature);
     l[i] = v;
     mt = fmaxf(mt, v);
@@ -424,7 +424,7 @@ __global__ void __cluster_dims__(kSmpCluster, 1, 1) __launch_bounds__(kSmpThread
   float best = -INFINITY;
   int idx = V;  // ties and all -inf rows: the first index wins
   for (int i = e0 + tid; i < e1; i += kSmpThreads) {
-    float v = s[i];
+    float v = __ldcg(s + i);
     if (!greedy && v > -INFINITY) {
       const uint64_t h = splitmix64(stream + (uint64_t)i);
       const float u = ((float)(h >> 40) + 0.5f) * 0x1p-24f;  // in (0, 1)
