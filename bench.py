@@ -10,13 +10,17 @@ synthetic (seeded): codes uniform 0..15, scales |N(0,1)|*0.002, biases -8*scale.
 launches carry programmatic-dependent-launch edges).  The weights total 4.46 GB, far
 above the 126 MB L2, so no flush is needed between steps.
 
-With --gpus N (torchrun, one rank per GPU) each projection is column-sharded: rank r
-owns a contiguous 1/N of the output rows (weights, scales, biases), and the shards are
-all-gathered after each projection (strong scaling: total work fixed).  By default the
-all-gather is fused into the qmv kernel (qvx_qmv_allgather: every rank stores its rows
-into every peer's inbox over NVLink as words tagged with the launch, and copies the
-peers' rows out of its own inbox; no NCCL call inside the step);
---gather nccl runs the local kernel followed by an NCCL all-gather instead.
+With --gpus N (torchrun, one rank per GPU) the step is tensor-parallel: the projections that
+feed a local nonlinearity (DeltaNet in_proj, attention q/k/v, MLP gate_up) keep 1/N of their
+output rows on each rank and exchange nothing; the projections that close a block (out_proj,
+o_proj, down) keep 1/N of their input columns and sum their partial outputs over the ranks;
+lm_head keeps 1/N of its rows and is gathered.  By default both exchanges run inside the qmv
+kernel (qvx_qmv_fused: partial sums, or output rows, stored into the peers' inboxes over
+NVLink as words tagged with the launch; no NCCL call inside the step), 65 per step;
+--gather nccl runs the local kernels followed by NCCL all-reduces / all-gathers instead.
+Strong scaling: the whole job's work is fixed.  After the timed region each rank checks
+lm_head bit for bit and a row-parallel projection against the unsharded kernel, and reads
+the device status word; the result goes into the JSON line.
 
 Prints ONE JSON line (rank 0).  `--impl reference` times the reference's arithmetic on
 the host CPU cores instead (the oracle port of engine/kernels.py's qmv arithmetic: MLX,
@@ -194,52 +198,78 @@ def measure_configs(torch, device, hbm_peak, tc_peak):
     return out
 
 
-def measure_model(torch, device, peak_gbs, decode_steps=256, prefill=4096, batch=64, batch_prefill=128):
+def measure_model(torch, device, peak_gbs, world=1, rank=0, dist=None, decode_steps=256, prefill=4096, batch=64,
+                  batch_prefill=128):
     """Model-level decode of a random-initialised Qwen3.5-9B-shaped 4-bit model (config 4):
     batch 1 after a `prefill`-token prompt (fed in 512-token chunks, as the reference's engine
     does), and `batch` sequences after `batch_prefill`-token prompts; greedy decode replayed
-    from one CUDA graph per step (tokens and position stay on the device).  Device-timed
-    with CUDA events; the weights (5 GB with the embedding) exceed L2."""
-    from qvex.qwen35 import Config, DecodeGraph, Qwen35
+    from one CUDA graph per step (tokens and position stay on the device).  With `world` > 1
+    the model is tensor-parallel (qvex.tp: heads and MLP slices per rank, row-parallel block
+    outputs summed inside the projection kernels for batch <= 8, by NCCL above).  Device-timed
+    with CUDA events, max over ranks; the weights (5 GB with the embedding) exceed L2."""
+    from qvex.qwen35 import Config, DecodeGraph, Qwen35, random_params
     from qvex.sampler import sample_pick, sample_scores
     from qvex.shapes import Qwen35Shape, qlinear_bytes
     cfg = Config.qwen35_9b()
-    model = Qwen35.random(cfg, seed=0, device=device)
+    if world > 1:
+        from qvex import tp as TPM
+        P = random_params(cfg, 0, device)
+        lcfg, LP = TPM.shard_params(cfg, P, world, rank)
+        del P
+        model = Qwen35.from_params(lcfg, LP)
+        TPM.attach(model, TPM.TP(None, world, rank, cfg.vocab_size))
+    else:
+        model = Qwen35.random(cfg, seed=0, device=device)
     weight_bytes = sum(qlinear_bytes(N, K) for _, N, K in Qwen35Shape().decode_linears())
     g = torch.Generator(device=device)
     g.manual_seed(5)
+
+    def max_ms(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     out = {}
     for B, P in ((1, prefill), (batch, batch_prefill)):
         cache = model.make_cache(capacity=P + decode_steps + 8)
         ids = torch.randint(0, cfg.vocab_size, (B, P), device=device, generator=g, dtype=torch.int64).to(torch.int32)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for c0 in range(0, P, 512):
             logits = model(ids[:, c0:c0 + 512].contiguous(), cache, last_only=True)
         e1.record()
         torch.cuda.synchronize()
-        prefill_ms = e0.elapsed_time(e1)
+        prefill_ms = max_ms(e0.elapsed_time(e1))
         first = sample_pick(sample_scores(logits.view(B, -1), temperature=0.0), True).view(B, 1)
         dg = DecodeGraph(model, cache, first, pos=P)
         n_warm = 3
         for _ in range(n_warm):
             dg.replay()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         e0.record()
         steps = decode_steps - n_warm
         for _ in range(steps):
             dg.replay()
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
+        ms = max_ms(e0.elapsed_time(e1)) / steps
         key = "batch1" if B == 1 else f"batch{B}"
         out[key] = {"tok_per_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4), "context": P,
                     "decode_steps": steps, "prefill_ms": round(prefill_ms, 1),
                     "prefill_tok_per_s": round(B * P / prefill_ms * 1e3, 1),
                     "weight_gbs": round(weight_bytes / ms / 1e6, 1),
-                    "frac_hbm_weights": round(weight_bytes / ms / 1e6 / peak_gbs, 3)}
+                    "frac_hbm_weights_per_gpu": round(weight_bytes / world / ms / 1e6 / peak_gbs, 3)}
         del dg, cache
+    if world > 1:
+        from qvex import tp as TPM
+        TPM.close(model)
     del model
     torch.cuda.empty_cache()
     return out
@@ -376,23 +406,40 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ workload
 
+ROW_PARALLEL = ("out_proj", "o_proj", "down")
+
+
 def build_weights(torch, shape, rank, world, device, seed=0):
-    """Synthetic 4-bit g64 weights of one decode step, rows sharded over `world` ranks."""
+    """Synthetic 4-bit g64 weights of one decode step, this rank's shard of each: with
+    `world` > 1 the projections that feed a local nonlinearity (DeltaNet in_proj, attention
+    q/k/v, MLP gate_up) keep 1/world of their output rows (column-parallel, no exchange), the
+    projections that close a block (out_proj, o_proj, down) keep 1/world of their input
+    columns (row-parallel, partial sums reduced over the ranks), and lm_head keeps 1/world of
+    its rows (gathered).  Returns (name, N, K, local QLinear, kind) per projection, kind in
+    "col", "row", "gather"."""
     from qvex.model import QLinear
     lins = []
     g = torch.Generator(device=device)
     for i, (name, N, K) in enumerate(shape.decode_linears()):
-        if N % world:
-            raise ValueError(f"{name}: N={N} does not split over {world} ranks")
-        n = N // world
+        kind = "col" if world == 1 else "row" if name.endswith(ROW_PARALLEL) else "gather" if name == "lm_head" else "col"
         g.manual_seed(seed * 100003 + i)
         # all 2^32 patterns equally likely => every 4-bit code uniform in 0..15
-        w = torch.randint(-2 ** 31, 2 ** 31, (N, K // 8), dtype=torch.int64, device=device, generator=g)
-        w = w.to(torch.int32)[rank * n:(rank + 1) * n].contiguous()
+        w = torch.randint(-2 ** 31, 2 ** 31, (N, K // 8), dtype=torch.int64, device=device, generator=g).to(torch.int32)
         s = (torch.randn((N, K // 64), device=device, generator=g).abs() * 0.002).to(torch.bfloat16)
-        s = s[rank * n:(rank + 1) * n].contiguous()
+        if kind == "row":
+            if K % (512 * world):
+                raise ValueError(f"{name}: K={K} does not split over {world} ranks in 512-column slices")
+            k = K // world
+            w = w[:, rank * k // 8:(rank + 1) * k // 8].contiguous()
+            s = s[:, rank * k // 64:(rank + 1) * k // 64].contiguous()
+        else:
+            if N % world:
+                raise ValueError(f"{name}: N={N} does not split over {world} ranks")
+            n = N // world
+            w = w[rank * n:(rank + 1) * n].contiguous()
+            s = s[rank * n:(rank + 1) * n].contiguous()
         b = (-8.0 * s.float()).to(torch.bfloat16)
-        lins.append((name, N, K, QLinear(w, s, b, 64, 4)))
+        lins.append((name, N, K, QLinear(w, s, b, 64, 4), kind))
     return lins
 
 
@@ -408,23 +455,34 @@ def full_linear(torch, shape, index, device, seed=0):
     return QLinear(w, s, b, 64, 4)
 
 
-def gather_check(torch, shape, lins, xs, full_out, world, device):
-    """After the timed replays: every rank recomputes a small (first k_proj) and the largest
-    (lm_head) projection unsharded with the single-GPU kernel and compares its gathered
-    output bit for bit (a row's arithmetic does not depend on how the rows are split).
-    Returns "ok" or the first mismatch."""
-    names = [n for n, _, _, _ in lins]
-    picks = [next(i for i, n in enumerate(names) if n.endswith("k_proj")), len(lins) - 1]
-    for i in picks:
-        name, N, K, _ = lins[i]
-        ref = full_linear(torch, shape, i, device)(xs[K])
-        got = full_out[i]
-        got = got.reshape(ref.shape) if got.dim() == 2 else got.permute(1, 0, 2).reshape(ref.shape)
-        torch.cuda.synchronize()
-        if not torch.equal(got.view(torch.int16), ref.view(torch.int16)):
-            bad = int((got.view(torch.int16) != ref.view(torch.int16)).sum())
-            return f"{name}: {bad} of {ref.numel()} outputs differ"
-        del ref
+def gather_check(torch, dist, shape, lins, xin, full_out, world, device):
+    """After the timed replays: every rank recomputes two projections unsharded with the
+    single-GPU kernel.  lm_head (gathered rows) must match bit for bit (a row's arithmetic
+    does not depend on how the rows are split); the first down projection (row-parallel,
+    partial sums reduced over the ranks in rank order) within rel-L2 1e-3 and bit-identical
+    on every rank.  Returns "ok" or the first mismatch."""
+    names = [l[0] for l in lins]
+    i_lm = len(lins) - 1
+    i_down = next(i for i, n in enumerate(names) if n.endswith("down"))
+    name, N, K, _, _ = lins[i_lm]
+    ref = full_linear(torch, shape, i_lm, device)(xin["full"][K])
+    got = full_out[i_lm]
+    got = got.reshape(ref.shape) if got.dim() == 2 else got.permute(1, 0, 2).reshape(ref.shape)
+    torch.cuda.synchronize()
+    if not torch.equal(got.view(torch.int16), ref.view(torch.int16)):
+        bad = int((got.view(torch.int16) != ref.view(torch.int16)).sum())
+        return f"{name}: {bad} of {ref.numel()} outputs differ"
+    del ref
+    name, N, K, _, _ = lins[i_down]
+    ref = full_linear(torch, shape, i_down, device)(xin["full"][K]).float()
+    got = full_out[i_down].reshape(ref.shape)
+    rel = float((got.float() - ref).norm() / ref.norm())
+    if rel > 1e-3:
+        return f"{name}: rel-L2 {rel:.2e} against the unsharded projection"
+    parts = [torch.empty_like(got) for _ in range(world)]
+    dist.all_gather(parts, got.contiguous())
+    if not all(torch.equal(p.view(torch.int16), parts[0].view(torch.int16)) for p in parts):
+        return f"{name}: the reduced output differs between ranks"
     return "ok"
 
 
@@ -455,36 +513,53 @@ def run_ours(args):
     shape = Qwen35Shape(layers=args.layers)
     M = args.m
     lins = build_weights(torch, shape, rank, world, device)
-    Ks = sorted({K for _, _, K, _ in lins})
+    Ks = sorted({K for _, _, K, _, _ in lins})
     g = torch.Generator(device=device)
     g.manual_seed(1234)
     xs = {K: torch.randn((M, K), device=device, generator=g).to(torch.bfloat16) for K in Ks}
-    local_out = [torch.empty((M, l.out_features), dtype=torch.bfloat16, device=device) for _, _, _, l in lins]
+    # row-parallel projections read this rank's slice of their input columns
+    xs_row = {K: xs[K][:, rank * (K // world):(rank + 1) * (K // world)].contiguous() for K in Ks}
+    xin = {"full": xs, "row": xs_row}
+    inputs = [xs_row[K] if kind == "row" else xs[K] for _, _, K, _, kind in lins]
+    local_out = [torch.empty((M, l.out_features), dtype=torch.bfloat16, device=device) for _, _, _, l, _ in lins]
     launches_per_step = len(lins)
     fused = world > 1 and args.gather == "fused"
     peer = None
     if fused:
-        # one output region per projection on every rank, mapped everywhere (CUDA IPC)
+        # lm_head's gather region and one reduce slot per row-parallel projection, mapped into
+        # every rank (CUDA IPC); the exchanges run inside the projection kernels
+        from qvex.core import qmv_fused
         from qvex.shard import PeerGather, qmv_allgather
-        peer = PeerGather([M * N * 2 for _, N, _, _ in lins])
-        descs = [peer.descriptor(i, N, rank * (N // world)) for i, (_, N, _, _) in enumerate(lins)]
-        full_out = [peer.output(i, M, N) for i, (_, N, _, _) in enumerate(lins)]
+        rows = [i for i, l in enumerate(lins) if l[4] == "row"]
+        i_lm = len(lins) - 1
+        peer = PeerGather([M * lins[i_lm][1] * 2], reduce=[(M, lins[i][1]) for i in rows])
+        gdesc = peer.descriptor(peer.reserve(), lins[i_lm][1], rank * (lins[i_lm][1] // world))
+        rdesc = {i: peer.reduce_descriptor(peer.reserve_reduce(), lins[i][1]) for i in rows}
+        full_out = [torch.empty((M, N), dtype=torch.bfloat16, device=device) if kind == "row" else
+                    peer.output(gdesc.slot, M, N) if kind == "gather" else None for _, N, _, _, kind in lins]
     else:
-        full_out = [torch.empty((world, M, N // world), dtype=torch.bfloat16, device=device) for _, N, _, _ in lins]
+        full_out = [torch.empty((M, N), dtype=torch.bfloat16, device=device) if kind == "row" else
+                    torch.empty((world, M, N // world), dtype=torch.bfloat16, device=device) if kind == "gather"
+                    else None for _, N, _, _, kind in lins]
 
     def step_qmv():
-        for (_, _, K, lin), out in zip(lins, local_out):
-            lin(xs[K], out=out)
+        for (_, _, K, lin, kind), x, out in zip(lins, inputs, local_out):
+            lin(x, out=out)
 
     def step_full():
-        if fused:
-            for (_, _, K, lin), d in zip(lins, descs):
-                qmv_allgather(lin, xs[K], d)
-            return
-        for (_, _, K, lin), out, full in zip(lins, local_out, full_out):
-            lin(xs[K], out=out)
-            if world > 1:
-                dist.all_gather_into_tensor(full, out)
+        for i, ((_, _, K, lin, kind), x, out) in enumerate(zip(lins, inputs, local_out)):
+            if kind == "col":
+                lin(x, out=out)
+            elif fused and kind == "row":
+                qmv_fused(x, lin.w, lin.scales, lin.biases, gather=rdesc[i], out=full_out[i])
+            elif fused:
+                qmv_allgather(lin, x, gdesc)
+            elif kind == "row":
+                lin(x, out=full_out[i])
+                dist.all_reduce(full_out[i])
+            else:
+                lin(x, out=out)
+                dist.all_gather_into_tensor(full_out[i], out)
 
     if args.profile:
         for _ in range(max(args.warmup, 1)):
@@ -539,9 +614,9 @@ def run_ours(args):
         clocks.stop()
     ms_q, _, _ = timed(graph_q, args.steps, 3) if world > 1 else (ms_total, t0, t1)
 
-    bytes_full = sum(qmv_bytes(M, N, K) for _, N, K, _ in lins)           # whole job, per step
-    bytes_rank = sum(qmv_bytes(M, N // world, K) for _, N, K, _ in lins)  # this rank's kernels
-    weight_bytes = sum(qlinear_bytes(N, K) for _, N, K, _ in lins)
+    bytes_full = sum(qmv_bytes(M, N, K) for _, N, K, _, _ in lins)            # whole job, per step
+    bytes_rank = sum(qmv_bytes(M, l.out_features, l.in_features) for _, _, _, l, _ in lins)  # this rank's
+    weight_bytes = sum(qlinear_bytes(N, K) for _, N, K, _, _ in lins)
     ms_step = ms_total / args.steps
     value = bytes_full / (ms_step * 1e-3) / 1e9
     achieved = bytes_rank / (ms_q / args.steps * 1e-3) / 1e9   # per-GPU qmv bytes / per-GPU qmv time
@@ -580,6 +655,8 @@ def run_ours(args):
             te0 = time.perf_counter()
         for K in Ks:
             xs[K].copy_(pin_x[K], non_blocking=True)
+            if world > 1:  # this rank's input columns of the row-parallel projections
+                xs_row[K].copy_(xs[K][:, rank * (K // world):(rank + 1) * (K // world)])
         graph_full.replay()
         pin_y.copy_(logits_dev, non_blocking=True)
         stream.synchronize()
@@ -597,22 +674,23 @@ def run_ours(args):
     if world > 1:
         graph_full.replay()
         torch.cuda.synchronize()
-        verdict = gather_check(torch, shape, lins, xs, full_out, world, device)
+        verdict = gather_check(torch, dist, shape, lins, xin, full_out, world, device)
         status = qvex._lib.device_status(torch.cuda.current_stream().cuda_stream)
         flags = [None] * world
         dist.all_gather_object(flags, (verdict, status))
         check = {"gather_check": "ok" if all(v == "ok" for v, _ in flags) else [v for v, _ in flags],
                  "device_status": max(st for _, st in flags),
-                 "checked": "first k_proj and lm_head, bit for bit against the unsharded kernel, every rank"}
+                 "checked": "lm_head (gathered) bit for bit and the first down (row-parallel, reduced) within "
+                            "rel-L2 1e-3 against the unsharded kernel on every rank, and bit-identical across ranks"}
 
     extra = {}
     if not args.no_extra and world == 1:
         for m2 in (2, 4, 8):
             xs2 = {K: torch.randn((m2, K), device=device, generator=g).to(torch.bfloat16) for K in Ks}
-            outs2 = [torch.empty((m2, l.out_features), dtype=torch.bfloat16, device=device) for _, _, _, l in lins]
+            outs2 = [torch.empty((m2, l.out_features), dtype=torch.bfloat16, device=device) for _, _, _, l, _ in lins]
 
             def step_m():
-                for (_, _, K, lin), out in zip(lins, outs2):
+                for (_, _, K, lin, _), out in zip(lins, outs2):
                     lin(xs2[K], out=out)
             step_m()
             torch.cuda.synchronize()
@@ -620,7 +698,7 @@ def run_ours(args):
             with torch.cuda.graph(gm):
                 step_m()
             ms_m, _, _ = timed(gm, max(args.steps // 4, 10), 3)
-            bm = sum(qmv_bytes(m2, N, K) for _, N, K, _ in lins)
+            bm = sum(qmv_bytes(m2, N, K) for _, N, K, _, _ in lins)
             extra[f"M={m2}"] = round(bm / (ms_m / max(args.steps // 4, 10) * 1e-3) / 1e9, 1)
             del gm
 
@@ -628,8 +706,8 @@ def run_ours(args):
     if world == 1 and not args.no_configs:
         configs = measure_configs(torch, device, peak, tc_peak())
     model_dec = None
-    if world == 1 and not args.no_model:
-        model_dec = measure_model(torch, device, peak)
+    if not args.no_model:
+        model_dec = measure_model(torch, device, peak, world, rank, dist)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -645,8 +723,11 @@ def run_ours(args):
             "config": {"workload": "config 1: all 145 4-bit g64 linears of one Qwen3.5-9B-shaped decode step",
                        "M": M, "layers": args.layers, "weight_bytes_per_step": weight_bytes,
                        "parallelism": ("single GPU" if world == 1 else
-                                       f"column-shard x{world} + all-gather fused into the qmv kernel (tagged inbox words over NVLink)"
-                                       if fused else f"column-shard x{world} + NCCL all-gather"),
+                                       f"tensor-parallel x{world}: in_proj/q/k/v/gate_up column-parallel (no exchange), "
+                                       "out_proj/o_proj/down row-parallel with the all-reduce fused into the qmv kernel, "
+                                       "lm_head gathered in-kernel (tagged words over NVLink; 65 exchanges per step)"
+                                       if fused else f"tensor-parallel x{world}: row-parallel projections all-reduced "
+                                       "and lm_head all-gathered by NCCL"),
                        "l2": "inputs larger than L2 (4.46 GB of weights per step)", "cuda_graph": True},
             "tok_per_s": round(1000.0 / ms_step, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -695,7 +776,7 @@ def _cpu_sample(torch, lins, xs, M, row_frac):
     """Host copies of the first `row_frac` of every linear's rows."""
     import numpy as np
     sample = []
-    for name, N, K, lin in lins:
+    for name, N, K, lin, _ in lins:
         n = max(8, int(lin.out_features * row_frac))
         w = lin.w[:n].cpu().numpy().view(np.uint32)
         s = lin.scales[:n].view(torch.int16).cpu().numpy().view(np.uint16)

@@ -288,10 +288,30 @@ class Layer:
         self.tp = None        # qvex.tp.TP when the layer is one rank's shard
         self.tp_desc = None   # (mixer output, MLP down) reduce descriptors for fused decode
 
+    def _row_parallel(self, lin: QLinear, xin: torch.Tensor, desc) -> torch.Tensor:
+        """A projection whose input columns may be sharded over ranks (out_proj, o_proj,
+        down_proj): one GPU computes it whole; sharded, each rank's partial sums are added
+        over the ranks -- inside the projection kernel for decode (qvx_qmv_fused with the
+        reduce exchange, B <= 8 rows), else by an NCCL all-reduce."""
+        if self.tp is None:
+            return lin(xin)
+        rows = xin.numel() // xin.shape[-1]
+        if desc is not None and rows <= 8:
+            y = qmv_fused(xin.reshape(rows, -1), lin.w, lin.scales, lin.biases, gather=desc,
+                          group_size=lin.group_size, bits=lin.bits)
+            return y.view(*xin.shape[:-1], -1)
+        return self.tp.all_reduce(lin(xin))
+
     def _mixer(self, n, cache, keep_prev, pos=None):
+        desc = self.tp_desc[0] if self.tp_desc is not None else None
         if self.linear:
-            return self.mixer.out_proj(self.mixer.mix(n, cache, keep_prev, inplace=pos is not None))
-        return self.mixer.o_proj(self.mixer.mix(n, cache, pos))
+            return self._row_parallel(self.mixer.out_proj, self.mixer.mix(n, cache, keep_prev, inplace=pos is not None),
+                                      desc)
+        return self._row_parallel(self.mixer.o_proj, self.mixer.mix(n, cache, pos), desc)
+
+    def _mlp(self, n2):
+        desc = self.tp_desc[1] if self.tp_desc is not None else None
+        return self._row_parallel(self.mlp.down, glue.swiglu(self.mlp.gate_up(n2)), desc)
 
     def forward_deferred(self, x: torch.Tensor, pending: torch.Tensor | None, cache, keep_prev: bool = False,
                          pos=None):
@@ -304,23 +324,22 @@ class Layer:
             n = glue.rms_norm(x, self.ln1, self.eps)
         else:
             n, x = glue.rms_norm(pending, self.ln1, self.eps, resid=x)
-        m = self._mixer(n, cache, keep_prev, pos)
-        if self.tp is not None:
-            self.tp.all_reduce(m)   # row-parallel out_proj / o_proj: sum the ranks' partials
+        m = self._mixer(n, cache, keep_prev, pos)   # summed over the ranks when sharded
         n2, h = glue.rms_norm(m, self.ln2, self.eps, resid=x)
-        mo = self.mlp(n2)
-        if self.tp is not None:
-            self.tp.all_reduce(mo)  # row-parallel down_proj
-        return h, mo
+        return h, self._mlp(n2)
 
     def __call__(self, x: torch.Tensor, cache, keep_prev: bool = False) -> torch.Tensor:
         h, mo = self.forward_deferred(x, None, cache, keep_prev)
         return glue.add(h, mo)
 
     def forward_fused(self, x: torch.Tensor, cache, pos: torch.Tensor) -> None:
-        """Decode form (B <= 8 tokens, one per sequence): the residual stream x [B, 1, H] is
-        updated in place, every norm, SwiGLU and residual add riding in the projections'
-        prologues and epilogues (qvx_qmv_fused).  Gives the same bits as forward_deferred."""
+        """Decode form with the glue fused into the projections (B <= 8 tokens, one per
+        sequence): the residual stream x [B, 1, H] is updated in place, every norm, SwiGLU and
+        residual add riding in the projections' prologues and epilogues (qvx_qmv_fused).  Gives
+        the same bits as forward_deferred.  Measured on B200 it is slower than the deferred
+        form with separate glue kernels (each CTA of a projection repeats the whole vector's
+        transform on its critical path, while a separate kernel overlaps the projection's
+        weight streaming), so decode_step uses it only when asked."""
         B = x.shape[0]
         x2 = x.view(B, -1)
         mx = self.mixer
@@ -385,18 +404,21 @@ class Qwen35:
                     raise ValueError("graph decode needs KV caches of fixed capacity (make_cache(capacity))")
                 c.reserve(B, layer.mixer.n_kv, layer.mixer.head_dim, 0, device)
 
-    def decode_step(self, ids: torch.Tensor, cache, pos: torch.Tensor, fused: bool | None = None) -> torch.Tensor:
+    def decode_step(self, ids: torch.Tensor, cache, pos: torch.Tensor, fused: bool = False) -> torch.Tensor:
         """One decode step of B sequences, ids [B, 1] int32 at the device position ``pos``
         (int32 [1]): every state updated in its own buffer and nothing read on the host, so the
         step can be captured once and replayed for every token.  Returns logits [B, 1, V].
-        With ``fused`` (default: wherever it applies, B <= 8) the norms, SwiGLU and residual
-        adds ride in the projection kernels (same bits, fewer launches)."""
+        With ``fused`` the norms, SwiGLU and residual adds ride in the projection kernels (same
+        bits, fewer launches; not the faster form on B200, see Layer.forward_fused)."""
         B = ids.shape[0]
-        if fused is None:
-            fused = all(l.fusable(B) for l in self.layers) and self.lm_head.in_features % 512 == 0
+        if fused and not (all(l.fusable(B) for l in self.layers) and self.lm_head.in_features % 512 == 0):
+            raise ValueError("the fused decode form needs B <= 8 and projections with K % 512 == 0")
         if not fused:
             x, pending = self.hidden(ids, cache, pos=pos)
             n = glue.rms_norm(pending, self.norm, self.cfg.rms_norm_eps, resid=x)[0]
+            if self.lm_desc is not None and B <= 8:  # sharded: vocabulary rows gathered in-kernel
+                _fused(self.lm_head, n.view(B, -1), "plain", gather=self.lm_desc)
+                return self.tp.peer.output(self.lm_desc.slot, B, self.lm_desc.n_total).view(B, 1, -1)
             return self._logits(n)
         x = self.embed(ids)  # [B, 1, H], the residual stream, updated in place below
         for layer, c in zip(self.layers, cache):
