@@ -125,6 +125,26 @@ def measure_configs(torch, device, hbm_peak, tc_peak):
     """Device-timed throughput of the config-2 and config-3 kernels with their rooflines."""
     import qvex
     out = {}
+    # config 0: one [12288, 4096] projection at M = 1 (28.3 MB of weights, inside L2), so six
+    # seeded weight copies (170 MB) rotate to make every launch stream from HBM
+    from qvex.model import QLinear
+    from qvex.shapes import qmv_bytes
+    g0 = torch.Generator(device=device)
+    g0.manual_seed(0)
+    N0, K0 = 12288, 4096
+    x0 = torch.randn((1, K0), device=device, generator=g0).to(torch.bfloat16)
+    copies = []
+    for _ in range(6):
+        w0 = torch.randint(-2 ** 31, 2 ** 31, (N0, K0 // 8), dtype=torch.int64, device=device, generator=g0)
+        s0 = (torch.randn((N0, K0 // 64), device=device, generator=g0).abs() * 0.002).to(torch.bfloat16)
+        copies.append(QLinear(w0.to(torch.int32), s0, (-8.0 * s0.float()).to(torch.bfloat16), 64, 4))
+    y0 = torch.empty((1, N0), dtype=torch.bfloat16, device=device)
+    it0 = iter(range(1 << 30))
+    ms = _cuda_time(torch, lambda: copies[next(it0) % 6](x0, out=y0), 60)
+    b0 = qmv_bytes(1, N0, K0)
+    out["qmv_config0"] = {"ms": round(ms, 5), "gbs": round(b0 / ms / 1e6, 1), "frac_hbm": round(b0 / ms / 1e6 / hbm_peak, 3),
+                          "bytes": b0, "note": "one launch per call, graph of 60 calls over 6 rotated weight copies"}
+    del copies
     c = config_cases(torch, device)
     M, N, K = c["M"], c["N"], c["K"]
     # quantize / pack: reads bf16 W, writes codes + scales + biases; two copies of W

@@ -129,3 +129,20 @@ def test_graph_decode_matches_eager_greedy(models):
     got = g.run(n)
     assert torch.equal(got, eager), (got, eager)
     assert all(c.offset == L + n for c in cache)
+
+
+def test_loaded_checkpoints_give_the_same_logits(tmp_path):
+    """A model loaded from an MLX-layout checkpoint directory (qvex.checkpoint.load_model) and
+    from the native .q35 file (load_q35) computes exactly the logits of the same parameters
+    built in memory."""
+    from qvex.checkpoint import load_model, load_q35, save_checkpoint, write_q35
+    from qvex.qwen35 import Qwen35, random_params
+    cfg = small_cfg()
+    P = random_params(cfg, 17, "cpu")
+    save_checkpoint(tmp_path / "mlx", cfg, P)
+    write_q35(tmp_path / "m.q35", cfg, P)
+    ids = torch.randint(0, cfg.vocab_size, (2, 9), device="cuda", dtype=torch.int32)
+    ref = Qwen35.from_params(cfg, {k: v.cuda() for k, v in P.items()})
+    want = host(ref(ids, ref.make_cache(), last_only=False))
+    for m in (load_model(tmp_path / "mlx"), load_q35(tmp_path / "m.q35")):
+        assert np.array_equal(host(m(ids, m.make_cache(), last_only=False)), want)
