@@ -177,9 +177,10 @@ __device__ __forceinline__ void make_planes(const uint32_t (&u)[16], XPlanes<PL>
   }
   int E = 0;
   if (mx > 0.0f && isfinite(mx)) frexpf(mx, &E);  // 2^(E-1) <= mx < 2^E
-  E = max(E, -100);                                // E <= 128, so both powers below are normal
+  E = max(E, -100);                                // E <= 128, so all powers below are normal
   const float up = __int_as_float((FB - E + 127) << 23);   // 2^(FB-E)
-  xp.scale = __int_as_float((E - FB + 127) << 23);         // 2^(E-FB)
+  // 2^(E-FB-4): the dot product loop produces 16 * sum(q * x_fix) (see its hi-nibble form)
+  xp.scale = __int_as_float((E - FB - 4 + 127) << 23);
   xp.xsum = sum;
 #pragma unroll
   for (int w = 0; w < 4; ++w)
@@ -390,19 +391,25 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
         const float sf = bf16_bits_to_f32(ssc[r * G + g]);
         const float bf = bf16_bits_to_f32(sbi[r * G + g]);
         const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
+        // even codes as bytes (w & 0x0F..), odd codes times 16 as bytes (w & 0xF0.., one
+        // LOP3 and no shift).  Per plane, the odd-code chain starts from the 1.5 * 2^23
+        // magic number and one LEA forms 16 * even + odd: the float bits of
+        // 1.5 * 2^23 + 16 * (plane sum), exact while that sum stays below 2^22 (unsigned
+        // planes: 16 * 15 * 255 * 32 < 2^21).  The factor 16 rides in xp.scale.
         uint32_t lo[4], hi[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          lo[j] = wd[j] & 0x0F0F0F0Fu;          // codes 8j + 0, 2, 4, 6
-          hi[j] = (wd[j] >> 4) & 0x0F0F0F0Fu;   // codes 8j + 1, 3, 5, 7
+          lo[j] = wd[j] & 0x0F0F0F0Fu;  // codes 8j + 0, 2, 4, 6
+          hi[j] = wd[j] & 0xF0F0F0F0u;  // 16 x codes 8j + 1, 3, 5, 7
         }
+        constexpr uint32_t kMagic = 0x4B400000u;
 #pragma unroll
         for (int m = 0; m < MC; ++m) {
-          float q;  // sum q * x_fix
+          float q;  // 16 * sum q * x_fix
           if constexpr (PL == 3) {
             // six independent chains (plane x even/odd codes), four DP4As deep
-            uint32_t a0l = 0, a1l = 0, a0h = 0, a1h = 0;
-            int a2l = 0, a2h = 0;
+            uint32_t a0l = 0, a1l = 0, a0h = kMagic, a1h = kMagic;
+            int a2l = 0, a2h = (int)kMagic;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               a0l = dp4a_uu(lo[j], xp[m].pl[0][2 * j], a0l);
@@ -412,14 +419,13 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
               a1h = dp4a_uu(hi[j], xp[m].pl[1][2 * j + 1], a1h);
               a2h = dp4a_us(hi[j], xp[m].pl[2][2 * j + 1], a2h);
             }
-            // |a| < 2^22: int -> float by the 1.5 * 2^23 magic number, exactly and off the XU pipe
-            const float f0 = __int_as_float(0x4B400000 + (int)(a0l + a0h)) - 12582912.0f;
-            const float f1 = __int_as_float(0x4B400000 + (int)(a1l + a1h)) - 12582912.0f;
-            const float f2 = __int_as_float(0x4B400000 + (a2l + a2h)) - 12582912.0f;
+            const float f0 = __uint_as_float((a0l << 4) + a0h) - 12582912.0f;
+            const float f1 = __uint_as_float((a1l << 4) + a1h) - 12582912.0f;
+            const float f2 = __int_as_float((int)((uint32_t)a2l << 4) + a2h) - 12582912.0f;
             q = fmaf(f2, 65536.0f, fmaf(f1, 256.0f, f0));
           } else {
-            uint32_t a0l = 0, a0h = 0;
-            int a1l = 0, a1h = 0;
+            uint32_t a0l = 0, a0h = kMagic;
+            int a1l = 0, a1h = (int)kMagic;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               a0l = dp4a_uu(lo[j], xp[m].pl[0][2 * j], a0l);
@@ -427,9 +433,9 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
               a0h = dp4a_uu(hi[j], xp[m].pl[0][2 * j + 1], a0h);
               a1h = dp4a_us(hi[j], xp[m].pl[1][2 * j + 1], a1h);
             }
-            const float f0 = __int_as_float(0x4B400000 + (int)(a0l + a0h)) - 12582912.0f;
-            const float f1 = __int_as_float(0x4B400000 + (a1l + a1h)) - 12582912.0f;
-            q = fmaf(f1, 256.0f, f0);  // exact: |q| < 2^22
+            const float f0 = __uint_as_float((a0l << 4) + a0h) - 12582912.0f;
+            const float f1 = __int_as_float((int)((uint32_t)a1l << 4) + a1h) - 12582912.0f;
+            q = fmaf(f1, 256.0f, f0);  // exact: 16 * an integer below 2^22 in magnitude
           }
           const float part = fmaf(sf * xp[m].scale, q, bf * xp[m].xsum);
           pv[i * MC + m] = FULLK ? part : (kact ? part : 0.0f);
@@ -660,11 +666,20 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   int* status = device_status_ptr();
   if (!status) return fail(QVX_ERR_CUDA, "qvx_qmv: device status word unavailable");
   const int P = (K + 1023) / 1024;
-  const int T = P >= 8 ? 1 : 8 / P;  // about 8 compute warps
-  // rows per team per stage: the most (4, 2 or 1) that keeps a stage's codes within 16 KB
+  // About 8 compute warps and 16 KB of codes per stage; projections of 64 MB of codes or
+  // more (a vocabulary head) take about 12 warps and 24 KB stages.  Measured on B200: the
+  // wide plan streams lm_head (N = 248320, K = 4096) at 5809 GB/s against 5156, but costs
+  // each launch ~0.9 us more (the bigger CTA), which smaller projections do not win back
+  // (break-even near 40 MB).  A row's arithmetic does not depend on the plan.
+  const bool wide = (size_t)N * K / 2 >= ((size_t)64 << 20);
+  const int target = wide ? kStreamMaxComputeWarps : 8;
+  const size_t stage_codes = wide ? kStreamStageCodeBytes * 3 / 2 : kStreamStageCodeBytes;
+  const int T = P >= target ? 1 : target / P;
+  // rows per team per stage: the most (4, 2 or 1) that keeps a stage's codes within the
+  // plan's size and a stage at 32 rows at most (the reducer's lanes take one row each)
   const int mc = M == 1 ? 1 : 2;  // tokens per CTA (x costs 26 registers per token)
   int rt = 4;
-  while (rt > 1 && (size_t)T * rt * K / 2 > kStreamStageCodeBytes) rt /= 2;
+  while (rt > 1 && ((size_t)T * rt * K / 2 > stage_codes || T * rt > 32)) rt /= 2;
   const bool fullk = K % 1024 == 0;
   // ring depth: as many stages (4..9) as the shared-memory budget holds
   int depth = (int)((kStreamSmemBudget - 16 - kStreamRowSsBytes) / (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)));
