@@ -95,6 +95,30 @@ __device__ __forceinline__ void pdl_grid_sync() {
   pdl_wait();
 }
 
+// Warp sum of V = 2^LV values per lane, transposed: at offset o the lanes with bit o set
+// keep the upper half of the remaining values and send the lower half, so after the first
+// LV offsets (16, 8, ...) value index bit k equals lane bit k + 5 - LV, and the remaining
+// offsets finish the sum.  Lane l ends with the warp-wide sum of value l >> (5 - LV) in
+// p[0] (V - 1 shuffles for V sums, plus 5 - LV for the replicas).
+template <int V, int OFF>
+__device__ __forceinline__ void reduce_transpose(float* p, int lane) {
+  if constexpr (OFF > 0) {
+    if constexpr (V > 1) {
+      const bool upper = (lane & OFF) != 0;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        const float send = upper ? p[i] : p[i + V / 2];
+        const float keep = upper ? p[i + V / 2] : p[i];
+        p[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+      }
+      reduce_transpose<V / 2, OFF / 2>(p, lane);
+    } else {
+      p[0] += __shfl_xor_sync(0xffffffffu, p[0], OFF);
+      reduce_transpose<1, OFF / 2>(p, lane);
+    }
+  }
+}
+
 // Launches `kern` with programmatic stream serialisation allowed (see pdl_grid_sync).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

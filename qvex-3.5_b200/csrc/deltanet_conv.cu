@@ -30,17 +30,18 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
     const __nv_bfloat16* state_in, __nv_bfloat16* state_out, __nv_bfloat16* state_mid, __nv_bfloat16* __restrict__ q,
     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v, __nv_bfloat16* __restrict__ a,
     __nv_bfloat16* __restrict__ b, int B, int T, int Hk, int Hv, float sc_q, float sc_k) {
-  pdl_grid_sync();
+  pdl_launch_dependents();
   constexpr int D = NPT * 32;
   constexpr int W = KW - 1;
   const int lane = threadIdx.x & 31;
   const int slots = 2 * Hk + Hv;
   const int nchunks = (T + kConvChunk - 1) / kConvChunk;
   const long long wid = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (wid >= (long long)B * slots * nchunks) return;
-  const int chunk = (int)(wid % nchunks);
-  const int slot = (int)((wid / nchunks) % slots);
-  const int bi = (int)(wid / ((long long)nchunks * slots));
+  const bool live = wid < (long long)B * slots * nchunks;
+  const long long wq = live ? wid : 0;
+  const int chunk = (int)(wq % nchunks);
+  const int slot = (int)((wq / nchunks) % slots);
+  const int bi = (int)(wq / ((long long)nchunks * slots));
   const int key_dim = Hk * D, value_dim = Hv * D;
   const int C = 2 * key_dim + value_dim;
   const int kind = slot < Hk ? 0 : slot < 2 * Hk ? 1 : 2;  // q, k, v head
@@ -48,11 +49,14 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
   const int ch0 = (kind == 0 ? 0 : kind == 1 ? key_dim : 2 * key_dim) + h * D + lane * NPT;
   const int t0 = chunk * kConvChunk, t1 = min(T, t0 + kConvChunk);
 
+  // the taps are constant: read before the upstream wait
   float wt[NPT][KW];
 #pragma unroll
   for (int i = 0; i < NPT; ++i)
 #pragma unroll
     for (int j = 0; j < KW; ++j) wt[i][j] = conv_w[(size_t)(ch0 + i) * KW + j];
+  pdl_wait();
+  if (!live) return;
 
   // conv_in row r: r < W -> state row r, else token r - W
   auto conv_in = [&](int r, float (&out)[NPT]) {
@@ -61,9 +65,12 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
 #pragma unroll
     for (int i = 0; i < NPT; ++i) out[i] = __bfloat162float(__ldcg(src + i));
   };
-  float win[W][NPT];
+  // the window and the first token's row in one round trip; each later row is requested a
+  // token ahead
+  float win[W][NPT], cur[NPT];
 #pragma unroll
   for (int j = 0; j < W; ++j) conv_in(t0 + j, win[j]);
+  conv_in(t0 + W, cur);
 
   auto store_window = [&](__nv_bfloat16* dst) {
 #pragma unroll
@@ -74,8 +81,8 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
 
   for (int t = t0; t < t1; ++t) {
     if (state_mid && t == T - 1) store_window(state_mid);
-    float cur[NPT];
-    conv_in(t + W, cur);
+    float nxt[NPT] = {};
+    if (t + 1 < t1) conv_in(t + 1 + W, nxt);
     float s[NPT];
 #pragma unroll
     for (int i = 0; i < NPT; ++i) {
@@ -92,7 +99,10 @@ __global__ void __launch_bounds__(128) deltanet_conv_kernel(
 #pragma unroll
       for (int i = 0; i < NPT; ++i) win[j][i] = win[j + 1][i];
 #pragma unroll
-    for (int i = 0; i < NPT; ++i) win[W - 1][i] = cur[i];
+    for (int i = 0; i < NPT; ++i) {
+      win[W - 1][i] = cur[i];
+      cur[i] = nxt[i];
+    }
 
     const size_t row = (size_t)bi * T + t;
     if (kind < 2) {

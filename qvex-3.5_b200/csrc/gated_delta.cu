@@ -113,16 +113,17 @@ __global__ void __launch_bounds__(kGdWarps * 32) gated_delta_kernel(
     const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, const float* __restrict__ A_log,
     const float* __restrict__ dt_bias, const float* state_in, __nv_bfloat16* __restrict__ y, float* state_out,
     float* __restrict__ state_mid, int T, int Hk, int Hv, int Dv) {
-  pdl_grid_sync();
+  pdl_launch_dependents();
   constexpr int Dk = NPT * 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n = blockIdx.y;  // b * Hv + hv
   const int bi = n / Hv, hv = n % Hv, hk = hv / (Hv / Hk);
   const int dv0 = (blockIdx.x * kGdWarps + warp) * kGdRowsPerWarp;
-  if (dv0 >= Dv) return;  // Dv % 16 == 0 is checked on the host, so whole warps exit
-
+  // the gate parameters are constant: read before the upstream wait
   const float A = expf(A_log[hv]);
   const float dt = dt_bias[hv];
+  pdl_wait();
+  if (dv0 >= Dv) return;  // Dv % 16 == 0 is checked on the host, so whole warps exit
 
   float st[kGdRowsPerWarp][NPT];
 #pragma unroll

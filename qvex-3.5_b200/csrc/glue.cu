@@ -49,34 +49,60 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&v)
 
 __device__ __forceinline__ float rbf16(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
 
+// 32 consecutive bf16 values as 16 raw words (value 2i in the low half of word i, 2i + 1 in
+// the high half); `upstream` as for load_bf16x32.
+__device__ __forceinline__ void load_raw32(const __nv_bfloat16* p, uint32_t (&u)[16], bool upstream) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 t = upstream ? __ldcg(q + c) : __ldg(q + c);
+    u[4 * c] = t.x; u[4 * c + 1] = t.y; u[4 * c + 2] = t.z; u[4 * c + 3] = t.w;
+  }
+}
+__device__ __forceinline__ float lo_f(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float hi_f(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
 // One CTA per row, one thread per 32 consecutive elements (D / 32 of them, D % 32 == 0), the
-// block rounded up to whole warps (threads past the row add zeros to the sums).
+// block rounded up to whole warps (threads past the row add zeros to the sums).  The weights
+// are read before the upstream wait and x and the residual together after it, so a row costs
+// one dependent round trip; values stay packed bf16 (registers at 1024 threads).
 // x, resid, h_out and out may alias (each thread reads its elements before it writes them).
 __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* resid,
                                                         const __nv_bfloat16* __restrict__ w, float eps,
                                                         __nv_bfloat16* h_out, __nv_bfloat16* out, int D) {
-  pdl_grid_sync();
+  pdl_launch_dependents();
   __shared__ float warp_sum[32];
   const size_t row = blockIdx.x;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
   const bool live = 32 * t < D;
-  float v[32];
+  uint32_t wr[16], hr[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) wr[i] = 0x3f803f80u;  // 1.0 pairs when there are no weights
+  if (w && live) load_raw32(w + 32 * t, wr, false);  // constant: before the upstream wait
+  pdl_wait();
   if (live) {
-    load_bf16x32(x + row * D + 32 * t, v);
+    load_raw32(x + row * D + 32 * t, hr, true);
+    if (resid) {
+      uint32_t rr[16];
+      load_raw32(resid + row * D + 32 * t, rr, true);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) hr[i] = pack_bf16x2(lo_f(hr[i]) + lo_f(rr[i]), hi_f(hr[i]) + hi_f(rr[i]));
+      if (h_out) {
+        uint4* q = reinterpret_cast<uint4*>(h_out + row * D + 32 * t);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) q[c] = make_uint4(hr[4 * c], hr[4 * c + 1], hr[4 * c + 2], hr[4 * c + 3]);
+      }
+    }
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-  }
-  if (resid && live) {
-    float r[32];
-    load_bf16x32(resid + row * D + 32 * t, r);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = rbf16(v[i] + r[i]);
-    if (h_out) store_bf16x32(h_out + row * D + 32 * t, v);
+    for (int i = 0; i < 16; ++i) hr[i] = 0u;
   }
   float s = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) s = fmaf(v[i], v[i], s);
+  for (int i = 0; i < 16; ++i) {
+    s = fmaf(lo_f(hr[i]), lo_f(hr[i]), s);
+    s = fmaf(hi_f(hr[i]), hi_f(hr[i]), s);
+  }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) warp_sum[warp] = s;
@@ -85,16 +111,18 @@ __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16* x, 
   for (int i = 1; i < nw; ++i) tot += warp_sum[i];
   const float r = 1.0f / sqrtf(tot / (float)D + eps);
   if (!live) return;
+  uint32_t o[16];
   if (w) {
-    float wv[32];
-    load_bf16x32(w + 32 * t, wv, false);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = wv[i] * rbf16(v[i] * r);
+    for (int i = 0; i < 16; ++i)
+      o[i] = pack_bf16x2(lo_f(wr[i]) * rbf16(lo_f(hr[i]) * r), hi_f(wr[i]) * rbf16(hi_f(hr[i]) * r));
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = v[i] * r;
+    for (int i = 0; i < 16; ++i) o[i] = pack_bf16x2(lo_f(hr[i]) * r, hi_f(hr[i]) * r);
   }
-  store_bf16x32(out + row * D + 32 * t, v);
+  uint4* q = reinterpret_cast<uint4*>(out + row * D + 32 * t);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) q[c] = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
 }
 
 // One thread per 32 consecutive elements of a head of D = 32 * L elements (L = 1, 2, 4, 8
@@ -104,7 +132,7 @@ __global__ void __launch_bounds__(256) gated_rms_norm_kernel(const __nv_bfloat16
                                                              const __nv_bfloat16* __restrict__ z, long long z_stride,
                                                              const __nv_bfloat16* __restrict__ w, float eps,
                                                              __nv_bfloat16* __restrict__ out, long long T, int H) {
-  pdl_grid_sync();
+  pdl_launch_dependents();
   constexpr int D = 32 * L;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long n = T * H * L;
@@ -114,17 +142,18 @@ __global__ void __launch_bounds__(256) gated_rms_norm_kernel(const __nv_bfloat16
   const int part = (int)(g % L);
   const long long t = head / H;
   const int h = (int)(head % H);
-  float v[32];
+  // weights before the upstream wait; y and z in one round trip after it
+  float wv[32], v[32], zv[32];
+  load_bf16x32(w + 32 * part, wv, false);
+  pdl_wait();
   load_bf16x32(y + head * D + 32 * part, v);
+  load_bf16x32(z + t * z_stride + (long long)h * D + 32 * part, zv);
   float s = 0.0f;
 #pragma unroll
   for (int i = 0; i < 32; ++i) s = fmaf(v[i], v[i], s);
 #pragma unroll
   for (int o = L / 2; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   const float r = 1.0f / sqrtf(s / (float)D + eps);
-  float zv[32], wv[32];
-  load_bf16x32(z + t * z_stride + (long long)h * D + 32 * part, zv);
-  load_bf16x32(w + 32 * part, wv, false);
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const float nrm = rbf16(wv[i] * rbf16(v[i] * r));

@@ -60,25 +60,6 @@ __host__ __device__ inline size_t stream_stage_bytes(int R, int K) {
   return (size_t)R * K / 2 + (size_t)R * K / 16 + 128u * kStreamMaxComputeWarps;
 }
 
-template <int V, int OFF>
-__device__ __forceinline__ void reduce_transpose(float* p, int lane) {
-  if constexpr (OFF > 0) {
-    if constexpr (V > 1) {
-      const bool upper = (lane & OFF) != 0;
-#pragma unroll
-      for (int i = 0; i < V / 2; ++i) {
-        const float send = upper ? p[i] : p[i + V / 2];
-        const float keep = upper ? p[i + V / 2] : p[i];
-        p[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
-      }
-      reduce_transpose<V / 2, OFF / 2>(p, lane);
-    } else {
-      p[0] += __shfl_xor_sync(0xffffffffu, p[0], OFF);
-      reduce_transpose<1, OFF / 2>(p, lane);
-    }
-  }
-}
-
 // Exchange of the sharded forms; world == 0 for the plain form.  A copy of qvx_gather in the
 // kernel's parameter space.  mode kExGather (column-sharded, qvx_qmv_allgather): out[rank]
 // is this rank's full bf16 output.  mode kExReduce (row-parallel, K sharded): out[rank] is

@@ -132,10 +132,10 @@ def attention_workspace(B: int, Hkv: int, G: int, L: int, D: int, nsplit: int, d
 
 
 def default_splits(B: int, Hkv: int, device=None) -> int:
-    """Key ranges per KV head for decode: about one CTA per SM over all (sequence, KV head)
-    pairs, at most 64 (each CTA streams its range in double-buffered 64-key tiles)."""
+    """Key ranges per KV head for decode: one CTA per SM at most over all (sequence, KV head)
+    pairs (a CTA of 8 warps, each warp streaming rounds of 8 keys), at most 64."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    return max(1, min(64, math.ceil(sms / max(1, B * Hkv))))
+    return max(1, min(64, sms // max(1, B * Hkv)))
 
 
 def attention(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor, eps: float, inv_freq: torch.Tensor,
