@@ -310,6 +310,25 @@ int qvx_deltanet_conv(const void* proj, long long proj_stride, const float* conv
                       const void* state_in, void* state_out, void* state_mid, void* q, void* k, void* v,
                       void* a, void* b, int B, int T, int Hk, int Hv, int Dk, int Dv, void* stream);
 
+/* GatedDeltaNet from the in_proj output to the out_proj input for up to 4 tokens per sequence
+ * (decode and the 2-token verify), in one launch: qvx_deltanet_conv, qvx_gated_delta and
+ * qvx_gated_rms_norm fused (engine/model.py:259-289 with engine/kernels.py:92-116), with
+ * their arithmetic, so that every output is bit-identical to the three-kernel path.
+ *   proj      bf16 [B, T, proj_stride]: qkv (C = 2 Hk Dk + Hv Dv) | z (Hv Dv) | b (Hv) | a (Hv)
+ *   conv_w    fp32 [C, conv_kernel] (conv_kernel 4)
+ *   conv_in   bf16 [B, 3, C] window; conv_out receives the new one (may be conv_in);
+ *             conv_mid, if not NULL, the window before the last token
+ *   A_log, dt_bias fp32 [Hv]; state_in fp32 [B, Hv, Dv, Dk]; state_out (may be state_in);
+ *             state_mid, if not NULL, the state before the last token
+ *   norm_w    bf16 [Dv] gated-norm weight, eps its epsilon
+ *   out       bf16 [B, T, Hv * Dv]
+ * Supported: T <= 4, Dk 64 or 128, (Hv / Hk) * (Dv / 32) == 8 (one 8-CTA cluster per key
+ * head); otherwise QVX_ERR_UNSUPPORTED and the caller runs the three kernels. */
+int qvx_deltanet_decode(const void* proj, long long proj_stride, const float* conv_w, int conv_kernel,
+                        const void* conv_in, void* conv_out, void* conv_mid, const float* A_log, const float* dt_bias,
+                        const float* state_in, float* state_out, float* state_mid, const void* norm_w, float eps,
+                        void* out, int B, int T, int Hk, int Hv, int Dk, int Dv, void* stream);
+
 /* Bytes of workspace qvx_attention's decode form needs (G = H / Hkv query heads per KV head,
  * G * L <= 8), or 0 when G * L > 8 (then the prefill form runs and needs none).  The
  * workspace must be zeroed once before its first use; the kernels leave it reusable. */

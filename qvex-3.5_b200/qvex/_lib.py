@@ -46,6 +46,8 @@ SIGNATURES = {
     "qvx_gated_rms_norm": (_I, [_P, _P, ctypes.c_longlong, _P, ctypes.c_float, _P, ctypes.c_longlong, _I, _I, _P]),
     "qvx_swiglu": (_I, [_P, ctypes.c_longlong, _P, ctypes.c_longlong, ctypes.c_longlong, _P]),
     "qvx_deltanet_conv": (_I, [_P, ctypes.c_longlong, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P] + [_I] * 6 + [_P]),
+    "qvx_deltanet_decode": (_I, [_P, ctypes.c_longlong, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_float, _P]
+                            + [_I] * 6 + [_P]),
     "qvx_attention_workspace_size": (_SZ, [_I] * 6),
     "qvx_attention": (_I, [_P, ctypes.c_longlong, _P, _P, ctypes.c_float, _P, _I, _P, _P, _I, _P, _I, _P, _P]
                       + [_I] * 5 + [ctypes.c_float, _P, _SZ, _I, _P]),

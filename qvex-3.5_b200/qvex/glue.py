@@ -3,7 +3,8 @@
 ``rms_norm`` (mx.fast.rms_norm, engine/model.py:314,316,335; with the residual add of
 :315-316 in front), ``gated_rms_norm`` (_gated_rmsnorm, :138-143), ``swiglu`` (_swiglu,
 :133-135), ``deltanet_conv`` (GatedDeltaNet.__call__ from the in_proj split to the
-gated_delta call, :259-277) and ``attention`` (Attention.__call__ between the projections,
+gated_delta call, :259-277), ``deltanet_decode`` (conv, recurrence and gated norm in one
+kernel for up to 4 tokens) and ``attention`` (Attention.__call__ between the projections,
 :213-232, with KVCache.update, :156-170).  Every call runs one libqvex entry point on the
 current CUDA stream; there is no other path.
 """
@@ -117,6 +118,52 @@ def deltanet_conv(proj: torch.Tensor, conv_w: torch.Tensor, state: torch.Tensor,
                                   _ptr(state_out), _ptr(mid), _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), B, T, Hk, Hv,
                                   Dk, Dv, _stream(proj)), "qvx_deltanet_conv")
     return (q, k, v, a, b, state_out, mid) if keep_mid else (q, k, v, a, b, state_out)
+
+
+def deltanet_decode_supported(T: int, Hk: int, Hv: int, Dk: int, Dv: int) -> bool:
+    """Whether qvx_deltanet_decode takes this shape (else run the three kernels)."""
+    return 1 <= T <= 4 and Dk in (64, 128) and Hv % Hk == 0 and Dv % 32 == 0 and (Hv // Hk) * (Dv // 32) == 8
+
+
+def deltanet_decode_preferred(B: int, T: int, Hk: int, Hv: int, Dk: int, Dv: int, device=None) -> bool:
+    """Whether to run the fused kernel: a supported shape whose B * Hk clusters of 8 CTAs
+    are resident at once (at most one per SM).  Measured on B200 at Qwen3.5-9B shapes: at
+    batch 1 (16 clusters) the fused kernel saves ~3 us per layer; at batch 64 (1024
+    clusters, several waves of a latency-bound kernel) it is far slower than the three
+    kernels, whose grids spread over the whole GPU."""
+    if not deltanet_decode_supported(T, Hk, Hv, Dk, Dv):
+        return False
+    return B * Hk <= torch.cuda.get_device_properties(device).multi_processor_count
+
+
+def deltanet_decode(proj: torch.Tensor, conv_w: torch.Tensor, conv_state: torch.Tensor, A_log: torch.Tensor,
+                    dt_bias: torch.Tensor, state: torch.Tensor, norm_w: torch.Tensor, eps: float, Hk: int, Hv: int,
+                    Dk: int, Dv: int, *, conv_out: torch.Tensor | None = None, state_out: torch.Tensor | None = None,
+                    keep_mid: bool = False, out: torch.Tensor | None = None):
+    """GatedDeltaNet from the in_proj output to the out_proj input in one kernel (T <= 4).
+    Returns (out [B, T, Hv*Dv], conv_out, state_out[, conv_mid, state_mid]); conv_out and
+    state_out may be the input buffers (in place)."""
+    _require_cuda("proj", proj, (torch.bfloat16,))
+    _require_cuda("conv_state", conv_state, (torch.bfloat16,))
+    _require_cuda("state", state, (torch.float32,))
+    B, T, S = proj.shape
+    if proj.stride(-1) != 1 or proj.stride(0) != T * proj.stride(1):
+        raise ValueError("proj rows must be evenly strided with unit stride along a row")
+    C, KW = conv_w.shape
+    dev = proj.device
+    if out is None:
+        out = torch.empty((B, T, Hv * Dv), dtype=torch.bfloat16, device=dev)
+    if conv_out is None:
+        conv_out = torch.empty_like(conv_state)
+    if state_out is None:
+        state_out = torch.empty_like(state)
+    cmid = torch.empty_like(conv_state) if keep_mid else None
+    smid = torch.empty_like(state) if keep_mid else None
+    check(lib().qvx_deltanet_decode(_ptr(proj), proj.stride(1), _ptr(conv_w.contiguous()), KW, _ptr(conv_state),
+                                    _ptr(conv_out), _ptr(cmid), _ptr(A_log), _ptr(dt_bias), _ptr(state), _ptr(state_out),
+                                    _ptr(smid), _ptr(norm_w), float(eps), _ptr(out), B, T, Hk, Hv, Dk, Dv,
+                                    _stream(proj)), "qvx_deltanet_decode")
+    return (out, conv_out, state_out, cmid, smid) if keep_mid else (out, conv_out, state_out)
 
 
 def rope_inv_freq(rotary_dim: int, base: float, device) -> torch.Tensor:

@@ -11,7 +11,8 @@ tensors in place of MLX arrays.  Every layer op runs a libqvex kernel:
   DeltaNet conv path    qvx_deltanet_conv                           :259-277
   recurrence            qvx_gated_delta                             :279-286
   gated rms_norm        qvx_gated_rms_norm                          :289-290
-  attention             qvx_attention (prep + split-key decode or prefill)   :213-232
+    (up to 4 tokens, while the clusters fit: the three in qvx_deltanet_decode)
+  attention             qvx_attention (one decode kernel, or prep + prefill)  :213-232
   SwiGLU                qvx_swiglu                                  :300-302
   residual add          qvx_add (or fused into the next rms_norm)   :316
   embedding             qvx_dequantize_rows                         :126-130
@@ -206,6 +207,10 @@ class Attention:
 class GatedDeltaNet:
     """Gated DeltaNet linear attention (engine/model.py:235-291)."""
 
+    # up to 4 tokens (decode, verify) in one kernel where the shape allows; False runs the
+    # three-kernel path (conv, recurrence, gated norm), which gives the same bits
+    fused_decode = True
+
     def __init__(self, cfg: Config, p: dict):
         self.cfg = cfg
         self.hk, self.hv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
@@ -236,6 +241,19 @@ class GatedDeltaNet:
         form a CUDA graph replays); otherwise new tensors replace them, as in the reference."""
         B, S, _ = x.shape
         proj = self.in_proj(x)
+        if self.fused_decode and glue.deltanet_decode_preferred(B, S, self.hk, self.hv, self.dk, self.dv, x.device):
+            # decode / verify: conv, recurrence and gated norm in one kernel (same bits)
+            if cache.conv is None:
+                self.init_state(cache, B, x.device)
+            r = glue.deltanet_decode(proj, self.conv_w, cache.conv, self.A_log, self.dt_bias, cache.ssm, self.norm_w,
+                                     self.cfg.rms_norm_eps, self.hk, self.hv, self.dk, self.dv,
+                                     conv_out=cache.conv if inplace else None, state_out=cache.ssm if inplace else None,
+                                     keep_mid=keep_prev)
+            out, cache.conv, cache.ssm = r[:3]
+            if keep_prev:
+                cache.conv_prev, cache.ssm_prev = r[3], r[4]
+            cache.offset += S
+            return out
         y = self.recur(proj, cache, keep_prev, inplace)
         z = proj.view(B * S, -1)[:, self.conv_dim:self.conv_dim + self.value_dim]
         return glue.gated_rms_norm(y, z, self.norm_w, self.cfg.rms_norm_eps).view(B, S, self.value_dim)
