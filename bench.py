@@ -64,7 +64,8 @@ def parse_args():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the config-2/3 kernel measurements (prefill qmm, quantize, gated DeltaNet)")
     ap.add_argument("--profile", nargs="?", const="step", default=None,
-                    choices=["step", "qmm", "qmm_small", "quantize", "gd_prefill", "gd_decode", "model_decode"],
+                    choices=["step", "qmm", "qmm_small", "quantize", "gd_prefill", "gd_decode", "model_decode",
+                             "attn_decode"],
                     help="run one case eagerly for a profiler (no graph, clocks or CPU baseline)")
     return ap.parse_args()
 
@@ -321,6 +322,25 @@ def profile_case(torch, device, case, reps):
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
         print(json.dumps({"profile_run": case, "reps": reps}))
+        return
+    if case == "attn_decode":
+        # one layer's decode attention: 1 sequence, 32 query / 8 KV heads of 128, 4096 cached
+        # positions (16.8 MB of keys and values), 18 key ranges (the model's split at B = 1)
+        from qvex import glue
+        H, Hkv, D, pos = 32, 8, 128, 4096
+        g = torch.Generator(device=device)
+        g.manual_seed(0)
+        qkv = torch.randn((1, 1, (2 * H + 2 * Hkv) * D), device=device, generator=g).to(torch.bfloat16)
+        kc = torch.randn((1, Hkv, pos + 64, D), device=device, generator=g).to(torch.bfloat16)
+        vc = torch.randn_like(kc)
+        qn = torch.ones(D, device=device, dtype=torch.bfloat16)
+        inv = glue.rope_inv_freq(32, 1e7, device)
+        ns = glue.default_splits(1, Hkv, device)
+        ws = glue.attention_workspace(1, Hkv, H // Hkv, 1, D, ns, device)
+        for _ in range(reps):
+            glue.attention(qkv, qn, qn, 1e-6, inv, kc, vc, pos, H, Hkv, D, workspace=ws, nsplit=ns)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_run": case, "reps": reps, "nsplit": ns}))
         return
     if case in ("qmm", "qmm_small"):
         c = config_cases(torch, device, small=(case == "qmm_small"))

@@ -170,6 +170,19 @@ enum qvx_qmv_prologue {
   QVX_IN_GATED_RMS_NORM = 3
 };
 
+/* Output form of a fused decode projection:
+ *   QVX_OUT_PLAIN          y bf16 [M, N] (with the residual epilogue when resid is set)
+ *   QVX_OUT_SWIGLU_PAIRS   the weight rows come in (gate, up) pairs -- row 2i is gate_i, row
+ *                          2i+1 is up_i (an MLP's gate|up projection with its rows
+ *                          interleaved) -- and y bf16 [M, N/2] receives
+ *                          y[m, i] = bf16(g * sigmoid(g) * u), g and u the bf16 projection
+ *                          outputs: qvx_swiglu fused into the projection, the same bits.
+ *                          N even; no residual and no exchange. */
+enum qvx_qmv_epilogue {
+  QVX_OUT_PLAIN = 0,
+  QVX_OUT_SWIGLU_PAIRS = 1
+};
+
 typedef struct qvx_qmv_io {
   int prologue;          /* enum qvx_qmv_prologue */
   long long x_stride;    /* elements between token rows of x; 0 means K (2K for SWIGLU) */
@@ -179,6 +192,7 @@ typedef struct qvx_qmv_io {
   int head_dim;          /* GATED_RMS_NORM: 32 .. 1024, a power of two dividing K */
   float eps;
   const void* resid;     /* epilogue residual or NULL */
+  int epilogue;          /* enum qvx_qmv_epilogue */
 } qvx_qmv_io;
 
 /* The decode projection (M <= 8, K % 512 == 0, K <= 12288) with a prologue and epilogue
@@ -294,6 +308,11 @@ int qvx_gated_rms_norm(const void* y, const void* z, long long z_stride, const v
  * at gu + m*gu_stride holding [gate (I) | up (I)] (the fused gate_up output,
  * engine/model.py:296,301-302).  I and gu_stride multiples of 8. */
 int qvx_swiglu(const void* gu, long long gu_stride, void* out, long long M, long long I, void* stream);
+
+/* The same over (gate, up) pairs: row m of gu holds g_0, u_0, g_1, u_1, ... (the gate|up
+ * projection with its weight rows interleaved, as QVX_OUT_SWIGLU_PAIRS uses them); out[m, i]
+ * = bf16(g_i * sigmoid(g_i) * u_i).  I and gu_stride multiples of 8. */
+int qvx_swiglu_pairs(const void* gu, long long gu_stride, void* out, long long M, long long I, void* stream);
 
 /* GatedDeltaNet.__call__ from the in_proj output to the recurrence inputs
  * (engine/model.py:259-277): split qkv|z|b|a, depthwise causal conv1d over [conv state;

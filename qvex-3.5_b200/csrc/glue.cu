@@ -184,6 +184,27 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
   *reinterpret_cast<uint4*>(out + m * I + c) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// The same over interleaved (gate, up) pairs: 8 outputs per thread from 16 consecutive values.
+__global__ void __launch_bounds__(256) swiglu_pairs_kernel(const __nv_bfloat16* __restrict__ gu, long long gu_stride,
+                                                           __nv_bfloat16* __restrict__ out, long long M, long long I) {
+  pdl_grid_sync();
+  const long long per_row = I / 8;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= M * per_row) return;
+  const long long m = gid / per_row, c = (gid % per_row) * 8;
+  const uint4* src = reinterpret_cast<const uint4*>(gu + m * gu_stride + 2 * c);
+  const uint4 a = __ldcg(src), b = __ldcg(src + 1);
+  const uint32_t pr[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};  // (g, u) in the low, high halves
+  float r[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float g = __uint_as_float(pr[j] << 16), u = __uint_as_float(pr[j] & 0xffff0000u);
+    r[j] = g * (1.0f / (1.0f + expf(-g))) * u;
+  }
+  *reinterpret_cast<uint4*>(out + m * I + c) = make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]),
+                                                          pack_bf16x2(r[4], r[5]), pack_bf16x2(r[6], r[7]));
+}
+
 // out = bf16(a + b), 8 elements per thread (the residual add h + mlp(h) of
 // engine/model.py:316 where no later kernel takes it over).
 __global__ void __launch_bounds__(256) add_kernel(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* out,
@@ -258,6 +279,21 @@ extern "C" int qvx_gated_rms_norm(const void* y, const void* z, long long z_stri
     default: launch_pdl(gated_rms_norm_kernel<16>, dim3(blocks), dim3(256), 0, s, yy, zz, z_stride, ww, eps, oo, T, H); break;
   }
   return check_launch("qvx_gated_rms_norm");
+}
+
+extern "C" int qvx_swiglu_pairs(const void* gu, long long gu_stride, void* out, long long M, long long I,
+                                void* stream) {
+  using namespace qvx;
+  if (M < 0 || I < 8 || I % 8 != 0 || gu_stride < 2 * I || gu_stride % 8 != 0)
+    return fail(QVX_ERR_INVALID, "qvx_swiglu_pairs: M=%lld I=%lld gu_stride=%lld (I and the stride multiples of 8)", M,
+                I, gu_stride);
+  if (!gu || !out) return fail(QVX_ERR_INVALID, "qvx_swiglu_pairs: null pointer");
+  if (!aligned(gu, 16) || !aligned(out, 16)) return fail(QVX_ERR_ALIGN, "qvx_swiglu_pairs: tensors need 16-byte alignment");
+  if (M == 0) return QVX_OK;
+  const long long n = M * (I / 8);
+  launch_pdl(swiglu_pairs_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(gu), gu_stride, static_cast<__nv_bfloat16*>(out), M, I);
+  return check_launch("qvx_swiglu_pairs");
 }
 
 extern "C" int qvx_swiglu(const void* gu, long long gu_stride, void* out, long long M, long long I, void* stream) {

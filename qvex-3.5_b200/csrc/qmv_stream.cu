@@ -81,7 +81,8 @@ struct QmvGather {
 //   kInSwiglu    silu(x[:, :K]) * x[:, K:2K] (qvx_swiglu; x is the gate|up output)
 //   kInGatedRms  x = y per head of 32 * head_lanes, rms_norm(y, norm_w) * silu(z)
 //                (qvx_gated_rms_norm; z row m at z + m * z_stride)
-// Epilogue: with resid, y = bf16(resid + bf16(acc)) (the residual add of a decoder layer).
+// Epilogue: with resid, y = bf16(resid + bf16(acc)) (the residual add of a decoder layer);
+// out_mode kOutSwigluPairs: qvx_swiglu over (gate, up) row pairs, y [M, N/2].
 constexpr int kInPlain = 0, kInRmsNorm = 1, kInSwiglu = 2, kInGatedRms = 3;
 struct QmvIO {
   int in_mode;
@@ -93,7 +94,9 @@ struct QmvIO {
   float eps;
   const __nv_bfloat16* resid;
   int x_bulk;  // 1: the CTA's x rows come into shared memory by one bulk copy (set by the host)
+  int out_mode;  // kOutPlain, or kOutSwigluPairs: rows (2i, 2i+1) = (gate_i, up_i) -> y[m, i] = silu(g) u
 };
+constexpr int kOutPlain = 0, kOutSwigluPairs = 1;
 
 __device__ __forceinline__ float rbf(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
 __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
@@ -477,6 +480,24 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       }
       if (!mbar_wait(&done[s], ph, abort_flag, status)) break;
       const float* red = reinterpret_cast<const float*>(stage(s) + (size_t)R * K / 2 + (size_t)R * K / 16);
+      if (io.out_mode == kOutSwigluPairs) {
+        // (gate, up) row pairs: the up value sits MC lanes further (rows start even, nr is
+        // even); qvx_swiglu's arithmetic on the two bf16 outputs
+#pragma unroll
+        for (int i = 0; i < kResPer; ++i) {
+          const int v = lane + 32 * i, r = v / MC, m = v % MC;
+          const bool ok = v < R * MC && r < nr && m < mc;
+          float acc = 0.0f;
+          if (ok) {
+            const int team = r / RT, idx = (r % RT) * MC + m;
+            for (int p = 0; p < P; ++p) acc += red[(team * P + p) * 32 + idx];
+          }
+          const float gv = __bfloat162float(__float2bfloat16_rn(acc));
+          const float uv = __shfl_down_sync(0xffffffffu, gv, MC);
+          if (ok && (r & 1) == 0)
+            y[(size_t)(m0 + m) * (N >> 1) + ((r0 + r) >> 1)] = __float2bfloat16_rn(gv * (1.0f / (1.0f + expf(-gv))) * uv);
+        }
+      } else
 #pragma unroll
       for (int i = 0; i < kResPer; ++i) {
         const int v = lane + 32 * i;
@@ -794,7 +815,12 @@ extern "C" int qvx_qmv_fused(const void* x, const uint32_t* w, const void* scale
     d_io.head_lanes = io->head_dim / 32;
     d_io.eps = io->eps;
     d_io.resid = static_cast<const __nv_bfloat16*>(io->resid);
+    d_io.out_mode = io->epilogue;
   }
+  if (d_io.out_mode != QVX_OUT_PLAIN && d_io.out_mode != QVX_OUT_SWIGLU_PAIRS)
+    return fail(QVX_ERR_INVALID, "%s: unknown epilogue %d", who, d_io.out_mode);
+  if (d_io.out_mode == QVX_OUT_SWIGLU_PAIRS && (N % 2 != 0 || d_io.resid || g))
+    return fail(QVX_ERR_INVALID, "%s: the SwiGLU-pairs epilogue needs an even N, no residual and no exchange", who);
   if (d_io.in_mode < QVX_IN_PLAIN || d_io.in_mode > QVX_IN_GATED_RMS_NORM)
     return fail(QVX_ERR_INVALID, "%s: unknown prologue %d", who, d_io.in_mode);
   if (M < 1 || M > 8 || N < 1 || K < 512 || K % 512 != 0 || K > kStreamMaxComputeWarps * 1024)

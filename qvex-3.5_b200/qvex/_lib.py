@@ -45,6 +45,7 @@ SIGNATURES = {
     "qvx_add": (_I, [_P, _P, _P, ctypes.c_longlong, _P]),
     "qvx_gated_rms_norm": (_I, [_P, _P, ctypes.c_longlong, _P, ctypes.c_float, _P, ctypes.c_longlong, _I, _I, _P]),
     "qvx_swiglu": (_I, [_P, ctypes.c_longlong, _P, ctypes.c_longlong, ctypes.c_longlong, _P]),
+    "qvx_swiglu_pairs": (_I, [_P, ctypes.c_longlong, _P, ctypes.c_longlong, ctypes.c_longlong, _P]),
     "qvx_deltanet_conv": (_I, [_P, ctypes.c_longlong, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P] + [_I] * 6 + [_P]),
     "qvx_deltanet_decode": (_I, [_P, ctypes.c_longlong, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_float, _P]
                             + [_I] * 6 + [_P]),
@@ -70,13 +71,15 @@ class QvxGather(ctypes.Structure):
 QVX_EXCHANGE_GATHER = 0
 QVX_EXCHANGE_REDUCE = 1
 QVX_IN_PLAIN, QVX_IN_RMS_NORM, QVX_IN_SWIGLU, QVX_IN_GATED_RMS_NORM = 0, 1, 2, 3
+QVX_OUT_PLAIN, QVX_OUT_SWIGLU_PAIRS = 0, 1  # enum qvx_qmv_epilogue
 
 
 class QvxQmvIO(ctypes.Structure):
     """Mirror of ``qvx_qmv_io`` (include/qvex.h): the prologue and epilogue of a fused
     decode projection."""
     _fields_ = [("prologue", _I), ("x_stride", ctypes.c_longlong), ("norm_w", _P), ("z", _P),
-                ("z_stride", ctypes.c_longlong), ("head_dim", _I), ("eps", ctypes.c_float), ("resid", _P)]
+                ("z_stride", ctypes.c_longlong), ("head_dim", _I), ("eps", ctypes.c_float), ("resid", _P),
+                ("epilogue", _I)]
 
 
 class QvexError(RuntimeError):

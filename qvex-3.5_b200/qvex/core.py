@@ -169,6 +169,7 @@ def dequantize_rows(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
 
 _PROLOGUES = {"plain": _lib.QVX_IN_PLAIN, "rms_norm": _lib.QVX_IN_RMS_NORM, "swiglu": _lib.QVX_IN_SWIGLU,
               "gated_rms_norm": _lib.QVX_IN_GATED_RMS_NORM}
+_EPILOGUES = {"plain": _lib.QVX_OUT_PLAIN, "swiglu_pairs": _lib.QVX_OUT_SWIGLU_PAIRS}
 
 
 def _rows(t: torch.Tensor, name: str) -> torch.Tensor:
@@ -181,12 +182,15 @@ def _rows(t: torch.Tensor, name: str) -> torch.Tensor:
 def qmv_fused(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
               prologue: str = "plain", norm_w: torch.Tensor | None = None, z: torch.Tensor | None = None,
               head_dim: int = 0, eps: float = 1e-6, resid: torch.Tensor | None = None,
-              out: torch.Tensor | None = None, gather=None, group_size: int = 64, bits: int = 4) -> torch.Tensor:
+              out: torch.Tensor | None = None, gather=None, group_size: int = 64, bits: int = 4,
+              epilogue: str = "plain") -> torch.Tensor:
     """Decode projection (M <= 8 token rows) with a fused prologue and residual epilogue
     (qvx_qmv_fused):  y = resid + (prologue(x) @ dequant(w)^T)  (resid optional), where the
     prologue is "plain", "rms_norm" (norm_w [K]), "swiglu" (x = gate|up rows of 2K) or
-    "gated_rms_norm" (per head of head_dim, norm_w [head_dim], z rows).  ``gather`` is a
-    qvx_gather descriptor (ctypes) for the sharded forms.  Returns y [M, N] (``out``)."""
+    "gated_rms_norm" (per head of head_dim, norm_w [head_dim], z rows).  epilogue
+    "swiglu_pairs": the weight rows are (gate, up) pairs and y [M, N/2] = silu(g) * u.
+    ``gather`` is a qvx_gather descriptor (ctypes) for the sharded forms.  Returns y
+    ([M, N], or [M, N/2]; ``out``)."""
     _check_qparams(group_size, bits)
     if prologue not in _PROLOGUES:
         raise ValueError(f"prologue must be one of {sorted(_PROLOGUES)}")
@@ -211,8 +215,11 @@ def qmv_fused(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: to
         if tuple(r2.shape) != (M, N) or not r2.is_contiguous():
             raise ValueError("resid must be a contiguous [M, N] bf16 tensor")
         io.resid = r2.data_ptr()
+    if epilogue not in _EPILOGUES:
+        raise ValueError(f"epilogue must be one of {sorted(_EPILOGUES)}")
+    io.epilogue = _EPILOGUES[epilogue]
     if out is None and not (gather is not None and gather.mode == _lib.QVX_EXCHANGE_GATHER):
-        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        out = torch.empty((M, N // 2 if epilogue == "swiglu_pairs" else N), dtype=torch.bfloat16, device=x.device)
     import ctypes
     check(lib().qvx_qmv_fused(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size, bits,
                               ctypes.byref(io), ctypes.byref(gather) if gather is not None else None, _stream(x2)),

@@ -91,6 +91,20 @@ def swiglu(gu: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor
     return out
 
 
+def swiglu_pairs(gu: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """gu [M, 2I] = (g_0, u_0, g_1, u_1, ...) (row stride gu.stride(0)) -> bf16 [M, I]:
+    SwiGLU of an MLP whose gate|up weight rows are interleaved in pairs."""
+    _require_cuda("gu", gu, (torch.bfloat16,))
+    g2 = gu.reshape(-1, gu.shape[-1]) if gu.dim() != 2 else gu
+    if g2.stride(-1) != 1:
+        raise ValueError("gu must have unit stride along its rows")
+    M, I2 = g2.shape
+    if out is None:
+        out = torch.empty((*gu.shape[:-1], I2 // 2), dtype=torch.bfloat16, device=gu.device)
+    check(lib().qvx_swiglu_pairs(_ptr(g2), g2.stride(0), _ptr(out), M, I2 // 2, _stream(gu)), "qvx_swiglu_pairs")
+    return out
+
+
 def deltanet_conv(proj: torch.Tensor, conv_w: torch.Tensor, state: torch.Tensor, Hk: int, Hv: int, Dk: int, Dv: int,
                   *, state_out: torch.Tensor | None = None, keep_mid: bool = False, outs=None):
     """proj [B, T, >= qkv|z|b|a] (in_proj output), conv_w fp32 [C, 4], state bf16 [B, 3, C].

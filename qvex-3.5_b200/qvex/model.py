@@ -46,6 +46,20 @@ class QLinear:
         )
 
 
+    @staticmethod
+    def interleave(a: "QLinear", b: "QLinear") -> "QLinear":
+        """One layer whose output rows alternate between ``a`` and ``b`` (a_0, b_0, a_1, b_1,
+        ...): an MLP's gate|up with SwiGLU applied to adjacent row pairs (qvx_qmv_fused's
+        swiglu_pairs epilogue, qvx_swiglu_pairs)."""
+        if a.w.shape != b.w.shape or (a.group_size, a.bits) != (b.group_size, b.bits):
+            raise AssertionError("interleaved layers must share the shape and the quantization")
+
+        def mix(x, y):
+            return torch.stack([x, y], dim=1).reshape(2 * x.shape[0], *x.shape[1:]).contiguous()
+
+        return QLinear(mix(a.w, b.w), mix(a.scales, b.scales), mix(a.biases, b.biases), a.group_size, a.bits)
+
+
 class QEmbedding:
     def __init__(self, w, scales, biases, group_size=64, bits=4):
         self.w, self.scales, self.biases = w, scales, biases

@@ -13,7 +13,7 @@ tensors in place of MLX arrays.  Every layer op runs a libqvex kernel:
   gated rms_norm        qvx_gated_rms_norm                          :289-290
     (up to 4 tokens, while the clusters fit: the three in qvx_deltanet_decode)
   attention             qvx_attention (one decode kernel, or prep + prefill)  :213-232
-  SwiGLU                qvx_swiglu                                  :300-302
+  SwiGLU                gate|up epilogue (decode) / qvx_swiglu_pairs  :300-302
   residual add          qvx_add (or fused into the next rms_norm)   :316
   embedding             qvx_dequantize_rows                         :126-130
 
@@ -283,15 +283,33 @@ class GatedDeltaNet:
 
 
 class MLP:
-    """SwiGLU MLP (engine/model.py:294-302)."""
+    """SwiGLU MLP (engine/model.py:294-302).  gate_proj and up_proj run as one projection
+    (the reference fuses them too, :296) with their rows interleaved in pairs (g_0, u_0, g_1,
+    u_1, ...): a decode batch (<= 8 rows) gets silu(g) * u straight from the projection's
+    epilogue (qvx_qmv_fused, swiglu_pairs), a prefill chunk from qvx_swiglu_pairs after the
+    matmul -- the same bits as [gate | up] followed by qvx_swiglu, one launch fewer per
+    decode layer."""
 
     def __init__(self, p: dict):
-        self.gate_up = QLinear.fuse([_qlin(p["gate_proj"]), _qlin(p["up_proj"])])
+        g, u = _qlin(p["gate_proj"]), _qlin(p["up_proj"])
+        self.gate_up = QLinear.interleave(g, u)
         self.down = _qlin(p["down_proj"])
-        self.hidden = _qlin(p["gate_proj"]).w.shape[0]
+        self.hidden = g.w.shape[0]
+
+    def act(self, x: torch.Tensor) -> torch.Tensor:
+        """silu(x @ gate^T) * (x @ up^T): x [..., H] -> [..., I]."""
+        x2 = x.reshape(-1, x.shape[-1])
+        gu = self.gate_up
+        if x2.shape[0] <= 8 and gu.in_features % 512 == 0 and gu.in_features <= 12288 and gu.group_size == 64 \
+                and gu.bits == 4:
+            y = qmv_fused(x2, gu.w, gu.scales, gu.biases, epilogue="swiglu_pairs", group_size=gu.group_size,
+                          bits=gu.bits)
+        else:
+            y = glue.swiglu_pairs(gu(x2))
+        return y.view(*x.shape[:-1], -1)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down(glue.swiglu(self.gate_up(x)))
+        return self.down(self.act(x))
 
 
 class Layer:
@@ -329,7 +347,7 @@ class Layer:
 
     def _mlp(self, n2):
         desc = self.tp_desc[1] if self.tp_desc is not None else None
-        return self._row_parallel(self.mlp.down, glue.swiglu(self.mlp.gate_up(n2)), desc)
+        return self._row_parallel(self.mlp.down, self.mlp.act(n2), desc)
 
     def forward_deferred(self, x: torch.Tensor, pending: torch.Tensor | None, cache, keep_prev: bool = False,
                          pos=None):
@@ -373,8 +391,8 @@ class Layer:
             qkv = _fused(mx.qkv, x2, "rms_norm", norm_w=self.ln1, eps=self.eps)
             o = mx.attend(qkv.view(B, 1, -1), cache, pos)
             _fused(mx.o_proj, o.view(B, -1), "plain", resid=x2, out=x2, gather=red_mix)
-        gu = _fused(self.mlp.gate_up, x2, "rms_norm", norm_w=self.ln2, eps=self.eps)
-        _fused(self.mlp.down, gu, "swiglu", resid=x2, out=x2, gather=red_down)
+        act = _fused(self.mlp.gate_up, x2, "rms_norm", norm_w=self.ln2, eps=self.eps, epilogue="swiglu_pairs")
+        _fused(self.mlp.down, act, "plain", resid=x2, out=x2, gather=red_down)
 
     def fusable(self, B: int) -> bool:
         """Whether forward_fused applies: B <= 8 and every projection's K a multiple of 512."""

@@ -114,3 +114,58 @@ def test_fused_decode_step_equals_unfused():
         assert same(a, b), f"step {step}"
         pos += 1
         tok = a.float().argmax(-1).to(torch.int32).view(B, 1)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 8])
+@pytest.mark.parametrize("N,K", [(24576, 4096), (2048, 512), (4096, 12288), (1024, 1536)])
+@pytest.mark.parametrize("prologue", ["plain", "rms_norm"])
+def test_swiglu_pairs_epilogue(M, N, K, prologue):
+    """The gate|up projection with its rows interleaved in (gate, up) pairs and SwiGLU in the
+    epilogue == the plain projection over the same rows followed by qvx_swiglu_pairs, and ==
+    the [gate | up] projection followed by qvx_swiglu (row order does not change a row)."""
+    import qvex
+    from qvex import glue
+    w, s, b = weights(N, K, 5 * M + N + K)
+    g = torch.Generator(device="cuda").manual_seed(M + 7)
+    x = (torch.randn((M, K), device="cuda", generator=g) * 2).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(K, device="cuda", generator=g)).to(torch.bfloat16)
+    kw = dict(norm_w=nw, eps=1e-6) if prologue == "rms_norm" else {}
+    got = qvex.core.qmv_fused(x, w, s, b, prologue=prologue, epilogue="swiglu_pairs", **kw)
+    xin = glue.rms_norm(x, nw, 1e-6) if prologue == "rms_norm" else x
+    y = qvex.quantized_matmul(xin, w, s, b)
+    assert got.shape == (M, N // 2)
+    assert same(got, glue.swiglu_pairs(y))
+    # the same rows de-interleaved into [gate | up] through qvx_swiglu
+    perm = torch.cat([torch.arange(0, N, 2), torch.arange(1, N, 2)]).cuda()
+    assert same(got, glue.swiglu(y[:, perm].contiguous()))
+
+
+def test_swiglu_pairs_epilogue_refusals():
+    import qvex
+    w, s, b = weights(2048, 512, 1)
+    x = torch.randn((1, 512), device="cuda").to(torch.bfloat16)
+    r = torch.zeros((1, 2048), device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        qvex.core.qmv_fused(x, w, s, b, epilogue="swiglu_pairs", resid=r)
+    w3, s3, b3 = weights(2047, 512, 2)
+    with pytest.raises(ValueError):
+        qvex.core.qmv_fused(x, w3, s3, b3, epilogue="swiglu_pairs")
+
+
+def test_mlp_interleaved_equals_reference_layout():
+    """The model's MLP (interleaved gate|up, SwiGLU in the epilogue at decode, qvx_swiglu_pairs
+    at prefill) gives the bits of [gate | up] -> qvx_swiglu -> down."""
+    import qvex
+    from qvex import glue
+    from qvex.model import QLinear
+    from qvex.qwen35 import MLP
+    H, I = 512, 1024
+    gw, gs, gb = weights(I, H, 11)
+    uw, us, ub = weights(I, H, 12)
+    dw, ds, db = weights(H, I, 13)
+    mlp = MLP({"gate_proj": (gw, gs, gb, 64, 4), "up_proj": (uw, us, ub, 64, 4), "down_proj": (dw, ds, db, 64, 4)})
+    ref_gu = QLinear.fuse([QLinear(gw, gs, gb, 64, 4), QLinear(uw, us, ub, 64, 4)])
+    for M in (1, 4, 40):
+        x = torch.randn((M, H), device="cuda", generator=torch.Generator(device="cuda").manual_seed(M)).to(torch.bfloat16)
+        ref = qvex.quantized_matmul(glue.swiglu(ref_gu(x)), dw, ds, db)
+        assert same(mlp(x), ref), M
