@@ -239,8 +239,13 @@ class GatedDeltaNet:
         """The out_proj input [B, S, Hv*Dv] (everything of __call__ but out_proj).  With
         ``inplace`` the conv window and recurrent state are updated in their own buffers (the
         form a CUDA graph replays); otherwise new tensors replace them, as in the reference."""
-        B, S, _ = x.shape
-        proj = self.in_proj(x)
+        return self.mix_proj(self.in_proj(x), cache, keep_prev, inplace)
+
+    def mix_proj(self, proj: torch.Tensor, cache: RecurrentCache, keep_prev: bool = False,
+                 inplace: bool = False) -> torch.Tensor:
+        """mix() from the in_proj output [B, S, *] on."""
+        B, S, _ = proj.shape
+        x = proj
         if self.fused_decode and glue.deltanet_decode_preferred(B, S, self.hk, self.hv, self.dk, self.dv, x.device):
             # decode / verify: conv, recurrence and gated norm in one kernel (same bits)
             if cache.conv is None:
@@ -383,10 +388,9 @@ class Layer:
         red_mix, red_down = self.tp_desc if self.tp_desc is not None else (None, None)
         if self.linear:
             proj = _fused(mx.in_proj, x2, "rms_norm", norm_w=self.ln1, eps=self.eps)
-            y = mx.recur(proj.view(B, 1, -1), cache, inplace=True)
-            z = proj[:, mx.conv_dim:mx.conv_dim + mx.value_dim]
-            _fused(mx.out_proj, y.view(B, -1), "gated_rms_norm", norm_w=mx.norm_w, z=z, head_dim=mx.dv,
-                   eps=self.eps, resid=x2, out=x2, gather=red_mix)
+            # conv, recurrence and gated norm (one kernel where the shape allows)
+            y = mx.mix_proj(proj.view(B, 1, -1), cache, inplace=True)
+            _fused(mx.out_proj, y.view(B, -1), "plain", resid=x2, out=x2, gather=red_mix)
         else:
             qkv = _fused(mx.qkv, x2, "rms_norm", norm_w=self.ln1, eps=self.eps)
             o = mx.attend(qkv.view(B, 1, -1), cache, pos)
@@ -587,7 +591,7 @@ class DecodeGraph:
     graph n times and returns the n x B tokens.  The caches must come from
     ``model.make_cache(capacity)``; states before the graph are kept (warm-up is undone)."""
 
-    def __init__(self, model: Qwen35, cache, first_ids: torch.Tensor, pos: int):
+    def __init__(self, model: Qwen35, cache, first_ids: torch.Tensor, pos: int, fused: bool = False):
         from .sampler import sample_pick, sample_scores
         self.model, self.cache = model, cache
         dev = first_ids.device
@@ -601,7 +605,7 @@ class DecodeGraph:
         self.hist = None
 
         def step():
-            logits = model.decode_step(self.ids, cache, self.pos)
+            logits = model.decode_step(self.ids, cache, self.pos, fused=fused)
             scores = sample_scores(logits.view(B, -1), temperature=0.0)
             sample_pick(scores, True, out=self.ids)
             self.pos.add_(1)
