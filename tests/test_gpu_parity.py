@@ -329,6 +329,29 @@ def test_gated_delta_in_place_state(qvex):
     assert torch.equal(s1, s2) and torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize("B,T,Hk,Hv,D", [(1, 40, 16, 32, 128), (3, 17, 4, 8, 64), (2, 100, 2, 4, 32)])
+def test_gated_delta_chunked_equals_per_step(qvex, B, T, Hk, Hv, D):
+    """T >= 16 runs the kernel that stages q, k, v, a, b through shared memory a chunk ahead;
+    a and b that are not 4-byte aligned take the per-step kernel instead.  Both give the same
+    bits (outputs, state, pre-last-step snapshot), with gates from A_log / dt_bias != 0."""
+    q, k, v, a, b, st = gd_inputs(B, T, Hk, Hv, D, D, 5 + T, "normal")
+    g = torch.Generator(device="cuda").manual_seed(T)
+    A_log = torch.randn(Hv, device="cuda", generator=g) * 0.5
+    dt = torch.randn(Hv, device="cuda", generator=g) * 0.5
+    state = torch.from_numpy(st).cuda()
+    ad, bd = dev(a), dev(b)
+    # the same values one bf16 element into a larger buffer: 2-byte aligned
+    a2 = torch.empty(ad.numel() + 1, dtype=torch.bfloat16, device="cuda")[1:].view(ad.shape)
+    b2 = torch.empty(bd.numel() + 1, dtype=torch.bfloat16, device="cuda")[1:].view(bd.shape)
+    a2.copy_(ad)
+    b2.copy_(bd)
+    assert a2.data_ptr() % 4 == 2
+    r1 = qvex.gated_delta(dev(q), dev(k), dev(v), ad, bd, A_log, dt, state, keep_mid=True)
+    r2 = qvex.gated_delta(dev(q), dev(k), dev(v), a2, b2, A_log, dt, state, keep_mid=True)
+    for x1, x2 in zip(r1, r2):
+        assert torch.equal(x1, x2)
+
+
 # ------------------------------------------------------------------ qmm (tensor cores, M > 8)
 
 def qmm_direct(qvex, x, w, s, b, short_by=0):
