@@ -213,9 +213,6 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
   __nv_bfloat16* x_s = reinterpret_cast<__nv_bfloat16*>(
       smem + ((S * stage_bytes + 3 * S * sizeof(uint64_t) + 16 + kStreamRowSsBytes + 127) & ~(size_t)127));
   __shared__ uint64_t xbar;
-  // rms_norm prologue: the norm weight [K] after the x rows, copied by the producer first
-  __nv_bfloat16* nw_s = x_s + (io.x_bulk ? (size_t)MC * K : 0);
-  __shared__ uint64_t wbar;
 
   const int m0 = blockIdx.y * MC;
   const int mc = min(MC, M - m0);
@@ -240,7 +237,6 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(&xbar, 1);
-    mbar_init(&wbar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -252,12 +248,6 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
   if (warp == NW - 2) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      // the norm weight ahead of the ring: read per lane it would queue behind the ring's
-      // ~180 KB (measured ~8000 cycles on the prologue's critical path)
-      if (io.in_mode == kInRmsNorm) {
-        mbar_arrive_expect_tx(&wbar, (uint32_t)K * 2u);
-        tma_bulk_g2s(nw_s, io.norm_w, (uint32_t)K * 2u, &wbar);
-      }
       int c = 0;
       for (; c < nchunks; ++c) {
         const int s = c % S;
@@ -306,8 +296,9 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     };
     // the norm weights do not come from the upstream kernel: in flight before the wait
     uint32_t wn[16];
-    // the gated norm's head weight (small, per lane); the rms_norm weight comes by bulk copy
-    ld16(io.norm_w + (lane % max(io.head_lanes, 1)) * 32, io.in_mode == kInGatedRms && kact, wn, false);
+    const bool has_w = io.in_mode == kInRmsNorm || io.in_mode == kInGatedRms;
+    ld16(io.in_mode == kInRmsNorm ? io.norm_w + (kact ? k0 : 0) : io.norm_w + (lane % max(io.head_lanes, 1)) * 32,
+         has_w && kact, wn, false);
     pdl_wait();  // x (and z, the gate|up rows, the residual) come from upstream kernels
     // x: one bulk copy of the CTA's rows into shared memory (x_bulk), which the teams then
     // share.  Measured on B200: when the upstream wait releases every CTA at once, the
@@ -342,13 +333,6 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
            has_aux && live, aux[m], true);
     }
     if (io.in_mode == kInRmsNorm) {
-      mbar_wait(&wbar, 0u, abort_flag, status);
-      const uint4* ws = reinterpret_cast<const uint4*>(nw_s + (kact ? k0 : 0));
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 t = kact ? ws[c] : make_uint4(0, 0, 0, 0);
-        wn[4 * c] = t.x; wn[4 * c + 1] = t.y; wn[4 * c + 2] = t.z; wn[4 * c + 3] = t.w;
-      }
       // the row's sum of squares: a lane's 32 inputs in order, a butterfly over the warp,
       // then the warps of the team in order (qvx_rms_norm's order)
 #pragma unroll
@@ -483,19 +467,6 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
     // ------------------------------------------------------------ reducer
     if (io.resid) pdl_wait();  // the residual comes from the upstream kernel
     constexpr int kResPer = (4 * 8 * MC + 31) / 32;  // residual values per lane per stage (R * MC <= 32 MC)
-    // The residual values of every chunk of this CTA in one round trip where they fit (a
-    // stage's load would otherwise put an L2 round trip into every stage of the reducer).
-    __shared__ float res_s[128];
-    const bool res_local = !(gather && g.mode == kExReduce);
-    const bool res_pre = io.resid && res_local && nchunks * R * MC <= 128;
-    if (res_pre) {
-      for (int v = lane; v < nchunks * R * MC; v += 32) {
-        const int c = v / (R * MC), rem = v % (R * MC), r = rem / MC, m = rem % MC;
-        const int r0 = chunk_row(c), nr = min(R, r_end - r0);
-        res_s[v] = (r < nr && m < mc) ? __bfloat162float(__ldcg(io.resid + (size_t)(m0 + m) * N + r0 + r)) : 0.0f;
-      }
-      __syncwarp();
-    }
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % S;
       const uint32_t ph = (uint32_t)(c / S) & 1u;
@@ -503,13 +474,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
       const int nr = min(R, r_end - r0);
       // the stage's residual values, loaded while the compute warps still work on it
       float resv[kResPer];
-      if (res_pre) {
-#pragma unroll
-        for (int i = 0; i < kResPer; ++i) {
-          const int v = lane + 32 * i;
-          resv[i] = v < R * MC ? res_s[c * R * MC + v] : 0.0f;
-        }
-      } else if (io.resid && res_local) {
+      if (io.resid && !(gather && g.mode == kExReduce)) {
 #pragma unroll
         for (int i = 0; i < kResPer; ++i) {
           const int v = lane + 32 * i, r = v / MC, m = v % MC;
@@ -677,7 +642,6 @@ __global__ void __launch_bounds__(32 * (kStreamMaxComputeWarps + 2), 1)
   }
   // the x copy has landed (it has unless a wait above gave up) before the CTA can exit
   if (io.x_bulk && threadIdx.x == 0) mbar_wait_drain(&xbar, 0u, status);
-  if (io.in_mode == kInRmsNorm && threadIdx.x == 0) mbar_wait_drain(&wbar, 0u, status);
   __syncthreads();
 }
 
@@ -690,9 +654,7 @@ static int launch_stream(int T, const void* x, const uint32_t* w, const void* s,
   const int R = T * RT;
   const size_t stage = stream_stage_bytes(R, K);
   size_t smem = S * stage + 3 * S * sizeof(uint64_t) + 16 + kStreamRowSsBytes;
-  if (io.x_bulk || io.in_mode == kInRmsNorm) smem = (smem + 127) & ~(size_t)127;
-  if (io.x_bulk) smem += (size_t)MC * K * 2;
-  if (io.in_mode == kInRmsNorm) smem += (size_t)K * 2;
+  if (io.x_bulk) smem = ((smem + 127) & ~(size_t)127) + (size_t)MC * K * 2;
   static bool attr_set[64] = {};  // per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -762,8 +724,7 @@ int qmv_stream_try(const void* x, const uint32_t* w, const void* s, const void* 
   // step unchanged (1.887 ms against 1.888).
   io.x_bulk = (io.in_mode == kInPlain || io.in_mode == kInRmsNorm) && T >= 2 && aligned(x, 16) &&
               (io.x_stride * 2) % 16 == 0;
-  const size_t x_area = (io.x_bulk || io.in_mode == kInRmsNorm ? 128 : 0) + (io.x_bulk ? (size_t)mc * K * 2 : 0) +
-                        (io.in_mode == kInRmsNorm ? (size_t)K * 2 : 0);
+  const size_t x_area = io.x_bulk ? 128 + (size_t)mc * K * 2 : 0;
   // ring depth: as many stages (4..9) as the shared-memory budget holds
   int depth = (int)((kStreamSmemBudget - 16 - kStreamRowSsBytes - x_area) /
                     (stream_stage_bytes(T * rt, K) + 3 * sizeof(uint64_t)));

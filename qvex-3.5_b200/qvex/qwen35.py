@@ -379,7 +379,8 @@ class Layer:
         residual add riding in the projections' prologues and epilogues (qvx_qmv_fused), the
         DeltaNet conv, recurrence and gated norm in one kernel.  Gives the same bits as
         forward_deferred with two launches fewer per layer; measured on B200 (batch 1, 4096
-        context, same box) 1.80 ms per token against 1.90-1.98 for the deferred form."""
+        context, same box) the two forms take the same time (1.81 against 1.80 ms per
+        token)."""
         B = x.shape[0]
         x2 = x.view(B, -1)
         mx = self.mixer
