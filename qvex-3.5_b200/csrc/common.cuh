@@ -32,11 +32,11 @@ int check_launch(const char* what);
 // device with cudaGetSymbolAddress and passed to kernels as an argument).
 int* device_status_ptr();
 
-// qvx_qmm's split of its tiles over the SMs (qmm_tc.cu): whole tiles first (F), then the
-// remaining tiles split into P parts along K with fp32 partial sums (part_bytes of
-// workspace); P = 1 means no split.
+// qvx_qmm's split of its tiles (bn tokens x 256 weight rows) over the SMs (qmm_tc.cu):
+// whole tiles first (F), then the remaining tiles split into P parts along K with fp32
+// partial sums (part_bytes of workspace); P = 1 means no split.
 struct QmmSplit {
-  int ntiles, F, P;
+  int ntiles, F, P, bn;
   size_t part_bytes;
 };
 QmmSplit qmm_split_plan(int M, int N, int K);

@@ -6,7 +6,8 @@
 //   B = x, fp16 (prepass in qmm.cu), staged by TMA into 128-byte-swizzled shared memory;
 //   D = fp32 accumulators in tensor memory, read back by tcgen05.ld in the epilogue.
 //
-// Tile: 256 weight rows (two M=128 MMAs into two accumulators) x 128 tokens (MMA N).
+// Tile: 256 weight rows (two M=128 MMAs into two accumulators) x 128 tokens (MMA N; 64
+// tokens when M <= 64).
 // One pipeline stage covers K = 128 (two quantisation groups): 16 MMAs of K=16, about
 // 1100 SM cycles of tensor work.  Every mbarrier operation costs one thread ~120 cycles
 // and a thread's operations run back to back, so a stage must carry enough MMA work to
@@ -17,7 +18,7 @@
 // partly filled round (all tiles at small M) are split along K over the idle SMs; their
 // parts' fp32 partial sums are added by qmm_tail_sum_kernel (qmm_split_plan).
 //
-// One ring of S stages, each holding the stage's x tile (2 x 16 KB), code tile (16 KB)
+// One ring of S stages, each holding the stage's x tile (2 x 16 KB, or 2 x 8 KB), code tile (16 KB)
 // and group multipliers (4 KB), filled by TMA (full[]) and released by ONE tcgen05
 // commit of the MMA thread (empty[s]) -- the dequantisers have read the codes before the
 // MMAs that release the stage could start.  The dequantised A tile has two tensor-memory
@@ -55,18 +56,7 @@ namespace qvx {
 namespace tc {
 
 constexpr int BM = 256;  // weight rows per tile
-constexpr int BN = 128;  // tokens per tile (MMA N)
 constexpr int BK = 128;  // K per stage (two groups)
-constexpr int S = 3;     // ring stages (shared memory)
-// "Data of step L landed" barriers: 2S of them, step L using full[L % (2S)].  A wait on a
-// barrier names only the parity of the phase it wants, and one still in the phase before
-// reads as complete for the next.  With one barrier per ring slot, a dequant group could
-// reach step L while the other group's step L - 3 (same slot, the phase before) had not
-// landed -- copies land out of order when a whole ring is issued at once -- and dequantise
-// step L - 3's codes; that was seen on B200.  With 2S barriers the phase before belongs to
-// step L - 6, which this group's own A-free wait at step L - 2 (the MMAs of step L - 4
-// are done) has already shown to have landed.
-constexpr int NFULL = 2 * S;
 constexpr int DQ_GROUPS = 2;
 constexpr int DQ_WARPS_PER_GROUP = 8;  // 2 halves x 4 lane quarters
 constexpr int NUM_DQ_WARPS = DQ_GROUPS * DQ_WARPS_PER_GROUP;
@@ -76,27 +66,49 @@ constexpr int WARP_MMA = 21;
 constexpr int THREADS = 22 * 32;
 static_assert(WARP_MMA == WARP_TMA + 1 && THREADS == (WARP_MMA + 1) * 32, "the MMA warp is the last warp");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t A_COL0 = 256;  // A stage a, half h: columns A_COL0 + (2a + h) * 64
-constexpr uint32_t X_HALF_BYTES = BN * 64 * 2;             // 16 KB: 128 tokens x 64 k, one swizzle span wide
-constexpr uint32_t X_BYTES = 2 * X_HALF_BYTES;              // 32 KB
-constexpr uint32_t CODE_BYTES = BM * (BK / 8) * 4;          // 16 KB: [256 rows][16 words], 64-byte swizzle
-constexpr uint32_t PRM_BYTES = BM * 2 * 8;                  // 4 KB: [256 rows][2 groups] x uint2
-constexpr uint32_t STAGE_BYTES = X_BYTES + CODE_BYTES + PRM_BYTES;
-static_assert(STAGE_BYTES % 1024 == 0, "stages keep 1024-byte alignment (swizzle atoms)");
+constexpr uint32_t A_COL0 = 256;                    // A stage a, half h: columns A_COL0 + (2a + h) * 64
+constexpr uint32_t CODE_BYTES = BM * (BK / 8) * 4;  // 16 KB: [256 rows][16 words], 64-byte swizzle
+constexpr uint32_t PRM_BYTES = BM * 2 * 8;          // 4 KB: [256 rows][2 groups] x uint2
 
-// shared memory layout (offsets from a 1024-byte aligned base)
-constexpr uint32_t OFF_CODE = X_BYTES;
-constexpr uint32_t OFF_PRM = X_BYTES + CODE_BYTES;
-constexpr uint32_t OFF_EPI = S * STAGE_BYTES;  // bf16 output tile [BN][BM] for the TMA store
-constexpr uint32_t EPI_BYTES = BN * BM * 2;    // 64 KB
-constexpr uint32_t OFF_BAR = OFF_EPI + EPI_BYTES;
-constexpr uint32_t NUM_BARS = NFULL + S + DQ_GROUPS + 5;
-constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
-constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+// Token-tile geometry.  BN tokens per tile (the MMA's N): 128, or 64 for small batches
+// (M <= 64, the decode of a batch), where a 128-token tile would spend half its tensor
+// work, x copies and partial sums on padding rows; the 64-token form has room for a
+// fourth ring stage.
+//
+// "Data of step L landed" barriers: 2S of them, step L using full[L % (2S)].  A wait on a
+// barrier names only the parity of the phase it wants, and one still in the phase before
+// reads as complete for the next.  With one barrier per ring slot, a dequant group could
+// reach step L while the other group's step L - S (same slot, the phase before) had not
+// landed -- copies land out of order when a whole ring is issued at once -- and dequantise
+// step L - S's codes; that was seen on B200.  With 2S barriers the phase before belongs to
+// step L - 2S, which this group's own A-free wait at step L - 2 (the MMAs of step L - 4
+// are done, S >= 2) has already shown to have landed.
+template <int BN_>
+struct Geo {
+  static constexpr int BN = BN_;
+  static constexpr int S = BN_ == 64 ? 4 : 3;  // ring stages (shared memory)
+  static constexpr int NFULL = 2 * S;
+  static constexpr uint32_t X_HALF_BYTES = BN * 64 * 2;  // BN tokens x 64 k, one swizzle span wide
+  static constexpr uint32_t X_BYTES = 2 * X_HALF_BYTES;
+  static constexpr uint32_t STAGE_BYTES = X_BYTES + CODE_BYTES + PRM_BYTES;
+  // shared memory layout (offsets from a 1024-byte aligned base)
+  static constexpr uint32_t OFF_CODE = X_BYTES;
+  static constexpr uint32_t OFF_PRM = X_BYTES + CODE_BYTES;
+  static constexpr uint32_t OFF_EPI = S * STAGE_BYTES;  // bf16 output tile [BN][BM] for the TMA store
+  static constexpr uint32_t EPI_BYTES = BN * BM * 2;
+  static constexpr uint32_t OFF_BAR = OFF_EPI + EPI_BYTES;
+  static constexpr uint32_t NUM_BARS = NFULL + S + DQ_GROUPS + 5;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+  // instruction descriptor: D f32, A f16, B f16, both K-major, N = BN, M = 128
+  static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  static_assert(BN == 64 || BN == 128, "token tiles of 64 or 128");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep 1024-byte alignment (swizzle atoms)");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
 
-// instruction descriptor: D f32, A f16, B f16, both K-major, N = 128, M = 128
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// Tokens per tile for M tokens.
+inline int token_tile(int M) { return M <= 64 ? 64 : 128; }
 
 __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
@@ -130,15 +142,19 @@ __device__ __forceinline__ void dequant_group(const uint4& c0, const uint4& c1, 
   }
 }
 
-template <bool kStaged>
+template <bool kStaged, int BN_>
 __global__ void __launch_bounds__(THREADS, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_y, const uint2* __restrict__ prm,
                   const int32_t* __restrict__ fexp, const int32_t* __restrict__ xexp, __nv_bfloat16* __restrict__ y,
                   int M, int N, int K, int n_pad, int F, int P, float* __restrict__ part, int* status) {
+  using G = Geo<BN_>;
+  constexpr int BN = G::BN, S = G::S, NFULL = G::NFULL;
+  constexpr uint32_t X_HALF_BYTES = G::X_HALF_BYTES, STAGE_BYTES = G::STAGE_BYTES, OFF_CODE = G::OFF_CODE,
+                     OFF_PRM = G::OFF_PRM, IDESC = G::IDESC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::OFF_BAR);
   uint64_t* full = bars;
   uint64_t* empty = full + NFULL;
   uint64_t* full_a = empty + S;
@@ -147,7 +163,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* drain = acc_empty + 1;
   uint64_t* epi_full = drain + 1;
   uint64_t* epi_free = epi_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::OFF_MISC);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -236,7 +252,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const bool storer = (warp == EPI_WARP0 && lane == 0);  // issues the tile's TMA store
-    uint16_t* stage_y = reinterpret_cast<uint16_t*>(smem + OFF_EPI);  // [BN tokens][BM rows] bf16
+    uint16_t* stage_y = reinterpret_cast<uint16_t*>(smem + G::OFF_EPI);  // [BN tokens][BM rows] bf16
     for (int lt = 0; lt < my_tiles; ++lt) {
       const int w = (int)blockIdx.x + lt * (int)gridDim.x, t = item_tile(w);
       float* part_p = w >= F ? part + (size_t)(w - F) * (BM * BN) : nullptr;
@@ -483,21 +499,22 @@ int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm
 }
 
 // y of the split tail tiles = bf16(sum of their P parts), in a fixed order (deterministic).
-// Element e of the parts' tile space: tile tt = e / (BM BN), token e / BM % BN, row e % BM.
+// Element e of the parts' tile space (bn tokens per tile): tile tt = e / (BM bn), token
+// e / BM % bn, row e % BM.
 __global__ void __launch_bounds__(256) qmm_tail_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ y,
-                                                           int M, int N, int F, int P, int ntail) {
-  using namespace tc;
-  const int tiles_m = (M + BN - 1) / BN;
-  const long long total = (long long)ntail * BM * BN;
+                                                           int M, int N, int F, int P, int ntail, int bn) {
+  using tc::BM;
+  const int tiles_m = (M + bn - 1) / bn, tile = BM * bn;
+  const long long total = (long long)ntail * tile;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-    const int tt = (int)(e / (BM * BN)), within = (int)(e % (BM * BN));
+    const int tt = (int)(e / tile), within = (int)(e % tile);
     const int t = F + tt, tok = within / BM, row = within % BM;
-    const int m = (t % tiles_m) * BN + tok, n = (t / tiles_m) * BM + row;
+    const int m = (t % tiles_m) * bn + tok, n = (t / tiles_m) * BM + row;
     if (m >= M || n >= N) continue;
-    const float* src = part + (size_t)tt * P * (BM * BN) + within;
+    const float* src = part + (size_t)tt * P * tile + within;
     float acc = src[0];
-    for (int p = 1; p < P; ++p) acc += src[(size_t)p * (BM * BN)];
+    for (int p = 1; p < P; ++p) acc += src[(size_t)p * tile];
     y[(size_t)m * N + n] = __float2bfloat16_rn(acc);
   }
 }
@@ -508,7 +525,8 @@ __global__ void __launch_bounds__(256) qmm_tail_sum_kernel(const float* __restri
 // parts, at least one stage each).  P = 1 (F = ntiles) when splitting gains nothing.
 QmmSplit qmm_split_plan(int M, int N, int K) {
   using namespace tc;
-  const int ntiles = ((M + BN - 1) / BN) * ((N + BM - 1) / BM);
+  const int bn = token_tile(M);
+  const int ntiles = ((M + bn - 1) / bn) * ((N + BM - 1) / BM);
   const int nks = (K + BK - 1) / BK;
   const int sms = num_sms();
   QmmSplit sp;
@@ -523,7 +541,8 @@ QmmSplit qmm_split_plan(int M, int N, int K) {
     P = 1;
   }
   sp.P = P;
-  sp.part_bytes = P > 1 ? (size_t)(ntiles - sp.F) * P * BM * BN * sizeof(float) : 0;
+  sp.bn = bn;
+  sp.part_bytes = P > 1 ? (size_t)(ntiles - sp.F) * P * BM * bn * sizeof(float) : 0;
   return sp;
 }
 
@@ -535,12 +554,14 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
   int* status = device_status_ptr();
   if (!status) return fail(QVX_ERR_CUDA, "qvx_qmm: device status word unavailable");
   const cuuint32_t estride[2] = {1, 1};
-  // x16 [M, K] fp16: 64 x 128 boxes, 128-byte swizzle (the MMA's K-major B layout); a
-  // box starting at K (odd group count) reads zeros
+  const int bn = sp.bn;
+  if (bn != token_tile(M)) return fail(QVX_ERR_INVALID, "qvx_qmm: split plan made for another batch size");
+  // x16 [M, K] fp16: 64 x bn boxes, 128-byte swizzle (the MMA's K-major B layout); a box
+  // starting at K (odd group count) reads zeros
   CUtensorMap tmap_x;
   const cuuint64_t xdim[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t xstride[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t xbox[2] = {64, BN};
+  const cuuint32_t xbox[2] = {64, (cuuint32_t)bn};
   CUresult r = enc(&tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), xdim, xstride, xbox, estride,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -555,7 +576,7 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QVX_ERR_CUDA, "qvx_qmm: w tensor map encode failed (%d)", (int)r);
-  // y [M, N] bf16 written by 256 x 128 TMA stores (clipped at the edges) when its rows are
+  // y [M, N] bf16 written by 256 x bn TMA stores (clipped at the edges) when its rows are
   // 16-byte multiples; otherwise the epilogue stores elements directly
   if (sp.P > 1 && !part) return fail(QVX_ERR_INVALID, "qvx_qmm: K parts need a partial-sum buffer");
   const int F = sp.P > 1 ? sp.F : sp.ntiles, P = sp.P > 1 ? sp.P : 1;
@@ -565,32 +586,35 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
   if (staged) {
     const cuuint64_t ydim[2] = {(cuuint64_t)N, (cuuint64_t)M};
     const cuuint64_t ystride[1] = {(cuuint64_t)N * 2};
-    const cuuint32_t ybox[2] = {BM, BN};
+    const cuuint32_t ybox[2] = {BM, (cuuint32_t)bn};
     r = enc(&tmap_y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, ydim, ystride, ybox, estride,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(QVX_ERR_CUDA, "qvx_qmm: y tensor map encode failed (%d)", (int)r);
   }
-  auto kern = staged ? qmm_tc_kernel<true> : qmm_tc_kernel<false>;
-  static bool attr_set[64][2] = {};
+  auto kern = bn == 64 ? (staged ? qmm_tc_kernel<true, 64> : qmm_tc_kernel<false, 64>)
+                       : (staged ? qmm_tc_kernel<true, 128> : qmm_tc_kernel<false, 128>);
+  const uint32_t smem = bn == 64 ? Geo<64>::SMEM_BYTES : Geo<128>::SMEM_BYTES;
+  const int variant = (bn == 64 ? 2 : 0) + (staged ? 1 : 0);
+  static bool attr_set[64][4] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev][staged]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+  if (dev < 0 || dev >= 64 || !attr_set[dev][variant]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return fail(QVX_ERR_CUDA, "qvx_qmm: cannot set shared memory size");
-    if (dev >= 0 && dev < 64) attr_set[dev][staged] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev][variant] = true;
   }
   const int nitems = F + (sp.ntiles - F) * P;
   const int grid = nitems < num_sms() ? nitems : num_sms();
-  kern<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap_x, tmap_w, tmap_y, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N), F, P,
-                                             P > 1 ? part : nullptr, status);
+  kern<<<grid, THREADS, smem, stream>>>(tmap_x, tmap_w, tmap_y, prm, fexp, xexp, y, M, N, K, qmm_row_pad(N), F, P,
+                                       P > 1 ? part : nullptr, status);
   int rc = check_launch("qvx_qmm");
   if (rc || P == 1) return rc;
   const int ntail = sp.ntiles - F;
-  const long long total = (long long)ntail * BM * BN;
+  const long long total = (long long)ntail * BM * bn;
   long long blocks = (total + 255) / 256;
   if (blocks > (long long)num_sms() * 8) blocks = (long long)num_sms() * 8;
-  qmm_tail_sum_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part, y, M, N, F, P, ntail);
+  qmm_tail_sum_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part, y, M, N, F, P, ntail, bn);
   return check_launch("qvx_qmm K-part sum");
 }
 

@@ -375,7 +375,7 @@ def qmm_direct(qvex, x, w, s, b, short_by=0):
 
 
 @pytest.mark.parametrize("M,N,K", [(9, 256, 64), (48, 384, 192), (130, 640, 320), (16, 256, 1024),
-                                   (64, 1024, 4096), (100, 300, 512),
+                                   (64, 1024, 4096), (100, 300, 512), (40, 300, 512), (63, 257, 2048),
                                    (129, 520, 1024), (256, 257, 2048), (512, 4096, 4096), (37, 12288, 4096),
                                    (200, 4096, 12288)])
 def test_qmm_matches_oracle(qvex, M, N, K):
