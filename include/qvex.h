@@ -80,6 +80,23 @@ int qvx_qmm(const void* x, const uint32_t* w, const void* scales, const void* bi
             void* y, int M, int N, int K, int group_size, int bits, void* workspace,
             size_t workspace_bytes, void* stream);
 
+/* The weight side of qvx_qmm's prepass, made once for a weight that stays constant (no
+ * counterpart in the reference, whose MLX kernel reads scales and biases directly): per
+ * weight row a power-of-two exponent, per group the fp16 multipliers the tensor-core
+ * kernel dequantises with.  qvx_qmm recomputes it on every call, an extra pass over
+ * scales and biases that costs about a fifth of a batch-64 decode projection.
+ * qvx_qmm_prepared_bytes: bytes of that buffer for an [N, K] weight (0 for a bad shape).
+ * qvx_qmm_prepare: writes it from scales/biases [N, K/64] bf16 into `prep` (256-byte
+ * aligned); redo it whenever the weight changes.
+ * qvx_qmm_prepared: qvx_qmm with the prepared buffer in place of scales and biases; the
+ * same results bit for bit, and a workspace of qvx_qmm_workspace_size(M, N, K) bytes is
+ * enough. */
+size_t qvx_qmm_prepared_bytes(int N, int K);
+int qvx_qmm_prepare(const void* scales, const void* biases, int N, int K, int group_size, int bits,
+                    void* prep, size_t prep_bytes, void* stream);
+int qvx_qmm_prepared(const void* x, const uint32_t* w, const void* prep, void* y, int M, int N, int K,
+                     int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream);
+
 /* qvx_qmm for callers that cannot allocate device memory: no counterpart in the
  * reference, which runs on MLX's own allocator.  It is meant for hosts that reach this
  * library only through the C ABI with no device allocator of their own, and for engines

@@ -42,13 +42,14 @@ struct QmmWorkspace {
   QmmSplit split;
 };
 
-static QmmWorkspace qmm_ws_layout(int M, int N, int K) {
+// prepared: the weight prepass (fexp, prm) lives in the caller's buffer, not here
+static QmmWorkspace qmm_ws_layout(int M, int N, int K, bool prepared = false) {
   QmmWorkspace l;
   l.off_x16 = 0;
   l.off_exp = align256((size_t)M * K * sizeof(__half));
   l.off_fexp = l.off_exp + align256((size_t)M * sizeof(int32_t));
-  l.off_prm = l.off_fexp + align256((size_t)N * sizeof(int32_t));
-  l.off_part = l.off_prm + align256(qmm_prm_bytes(N, K));
+  l.off_prm = l.off_fexp + (prepared ? 0 : align256((size_t)N * sizeof(int32_t)));
+  l.off_part = l.off_prm + (prepared ? 0 : align256(qmm_prm_bytes(N, K)));
   l.base = l.off_part;
   l.split = qmm_split_plan(M, N, K);
   l.total = l.split.P > 1 ? l.off_part + align256(l.split.part_bytes) : l.base;
@@ -112,9 +113,16 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const __nv_bfloat16* __re
   if (threadIdx.x == 0) xexp[m] = e;
 }
 
-int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
-                int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  const QmmWorkspace l = qmm_ws_layout(M, N, K);
+// The weight prepass of an [N, K] weight in a caller's buffer: fexp [N] int32, then prm at
+// a 256-byte boundary.
+static size_t prep_off_prm(int N) { return align256((size_t)N * sizeof(int32_t)); }
+
+// prep_fexp / prep_prm: a weight prepass made once by qvx_qmm_prepare (null: made here)
+static int qmm_run(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
+                   int K, void* workspace, size_t workspace_bytes, cudaStream_t stream, const int32_t* prep_fexp,
+                   const uint2* prep_prm) {
+  const bool prepared = prep_fexp != nullptr;
+  const QmmWorkspace l = qmm_ws_layout(M, N, K, prepared);
   if (!workspace || workspace_bytes < l.base)
     return fail(QVX_ERR_WORKSPACE, "qvx_qmm: workspace of %zu bytes needed, %zu given", l.total,
                 workspace ? workspace_bytes : (size_t)0);
@@ -128,15 +136,22 @@ int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void
   char* ws = static_cast<char*>(workspace);
   __half* x16 = reinterpret_cast<__half*>(ws + l.off_x16);
   int32_t* xexp = reinterpret_cast<int32_t*>(ws + l.off_exp);
-  int32_t* fexp = reinterpret_cast<int32_t*>(ws + l.off_fexp);
-  uint2* prm = reinterpret_cast<uint2*>(ws + l.off_prm);
+  int32_t* fexp = prepared ? const_cast<int32_t*>(prep_fexp) : reinterpret_cast<int32_t*>(ws + l.off_fexp);
+  uint2* prm = prepared ? const_cast<uint2*>(prep_prm) : reinterpret_cast<uint2*>(ws + l.off_prm);
   x_to_f16_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), x16, xexp, K);
   int rc = check_launch("qvx_qmm prepass");
   if (rc) return rc;
-  rc = qmm_w_prep(scales, biases, fexp, prm, N, K, stream);
-  if (rc) return rc;
+  if (!prepared) {
+    rc = qmm_w_prep(scales, biases, fexp, prm, N, K, stream);
+    if (rc) return rc;
+  }
   float* part = split.P > 1 ? reinterpret_cast<float*>(ws + l.off_part) : nullptr;
   return qmm_tc_launch(x16, xexp, fexp, prm, w, static_cast<__nv_bfloat16*>(y), M, N, K, split, part, stream);
+}
+
+int qmm_checked(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int M, int N,
+                int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return qmm_run(x, w, scales, biases, y, M, N, K, workspace, workspace_bytes, stream, nullptr, nullptr);
 }
 
 }  // namespace qvx
@@ -161,6 +176,41 @@ extern "C" int qvx_qmm(const void* x, const uint32_t* w, const void* scales, con
   if (rc) return rc;
   return qvx::qmm_checked(x, w, scales, biases, y, M, N, K, workspace, workspace_bytes,
                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t qvx_qmm_prepared_bytes(int N, int K) {
+  if (N < 1 || K < 64 || K % 64 != 0) return 0;
+  return qvx::prep_off_prm(N) + qvx::align256(qvx::qmm_prm_bytes(N, K));
+}
+
+extern "C" int qvx_qmm_prepare(const void* scales, const void* biases, int N, int K, int group_size, int bits,
+                               void* prep, size_t prep_bytes, void* stream) {
+  using namespace qvx;
+  if (group_size != 64 || bits != 4)
+    return fail(QVX_ERR_UNSUPPORTED, "qvx_qmm_prepare: only bits=4, group_size=64 is implemented (got bits=%d, "
+                "group_size=%d)", bits, group_size);
+  if (N < 1 || K < 64 || K % 64 != 0)
+    return fail(QVX_ERR_INVALID, "qvx_qmm_prepare: bad shape N=%d K=%d (K must be a positive multiple of 64)", N, K);
+  if (!scales || !biases || !prep) return fail(QVX_ERR_INVALID, "qvx_qmm_prepare: null pointer");
+  if (!aligned(scales, 2) || !aligned(biases, 2) || !aligned(prep, 256))
+    return fail(QVX_ERR_ALIGN, "qvx_qmm_prepare: scales/biases 2-byte and prep 256-byte aligned");
+  const size_t need = qvx_qmm_prepared_bytes(N, K);
+  if (prep_bytes < need)
+    return fail(QVX_ERR_WORKSPACE, "qvx_qmm_prepare: %zu bytes needed, %zu given", need, prep_bytes);
+  char* p = static_cast<char*>(prep);
+  return qmm_w_prep(scales, biases, reinterpret_cast<int32_t*>(p), reinterpret_cast<uint2*>(p + prep_off_prm(N)), N, K,
+                    static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qvx_qmm_prepared(const void* x, const uint32_t* w, const void* prep, void* y, int M, int N, int K,
+                                int group_size, int bits, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace qvx;
+  int rc = check_qparams("qvx_qmm_prepared", x, w, prep, prep, y, M, N, K, group_size, bits);
+  if (rc) return rc;
+  if (!aligned(prep, 256)) return fail(QVX_ERR_ALIGN, "qvx_qmm_prepared: prep must be 256-byte aligned");
+  const char* p = static_cast<const char*>(prep);
+  return qmm_run(x, w, nullptr, nullptr, y, M, N, K, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                 reinterpret_cast<const int32_t*>(p), reinterpret_cast<const uint2*>(p + prep_off_prm(N)));
 }
 
 extern "C" int qvx_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases,

@@ -33,6 +33,9 @@ SIGNATURES = {
     "qvx_qmm_workspace_size": (_SZ, [_I, _I, _I]),
     "qvx_qmm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "qvx_qmm_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "qvx_qmm_prepared_bytes": (_SZ, [_I, _I]),
+    "qvx_qmm_prepare": (_I, [_P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    "qvx_qmm_prepared": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "qvx_qmv_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "qvx_qmv_fused": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "qvx_quantized_matmul": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),

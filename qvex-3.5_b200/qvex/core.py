@@ -53,15 +53,37 @@ def qmm_workspace_size(M: int, N: int, K: int) -> int:
     return int(lib().qvx_qmm_workspace_size(M, N, K))
 
 
+def qmm_prepare(scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64, bits: int = 4) -> torch.Tensor:
+    """The tensor-core kernel's weight prepass (per-row exponents, per-group fp16
+    multipliers) of a constant weight, made once: a uint8 device buffer to pass to
+    quantized_matmul as ``prep``."""
+    _check_qparams(group_size, bits)
+    _require_cuda("scales", scales, (torch.bfloat16,))
+    _require_cuda("biases", biases, (torch.bfloat16,))
+    if scales.dim() != 2 or tuple(biases.shape) != tuple(scales.shape):
+        raise ValueError("scales and biases must be 2-D of one shape")
+    N, G = scales.shape
+    K = G * group_size
+    scales = scales.contiguous()
+    biases = biases.contiguous()
+    nbytes = int(lib().qvx_qmm_prepared_bytes(N, K))
+    prep = torch.empty(nbytes, dtype=torch.uint8, device=scales.device)
+    check(lib().qvx_qmm_prepare(_ptr(scales), _ptr(biases), N, K, group_size, bits, _ptr(prep), nbytes,
+                                _stream(scales)), "qvx_qmm_prepare")
+    return prep
+
+
 def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                      transpose: bool = True, group_size: int = 64, bits: int = 4, *,
                      out: torch.Tensor | None = None,
-                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+                     workspace: torch.Tensor | None = None,
+                     prep: torch.Tensor | None = None) -> torch.Tensor:
     """y[..., N] = x[..., K] @ dequant(w)^T (mx.quantized_matmul with transpose=True).
 
     M = prod(x.shape[:-1]) <= 8 runs the SIMT decode kernel, larger M the tcgen05
     tensor-core kernel (which needs a workspace; one is taken from the caching
-    allocator when none is given).
+    allocator when none is given).  ``prep`` (from qmm_prepare of these scales and
+    biases) spares the tensor-core path its per-call weight prepass; same results.
     """
     _check_qparams(group_size, bits)
     if not transpose:
@@ -98,9 +120,17 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
         need = qmm_workspace_size(M, N, K)
         if workspace is None:
             workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
-        check(lib().qvx_qmm(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size,
-                            bits, _ptr(workspace), workspace.numel() * workspace.element_size(), s),
-              "qvx_qmm")
+        if prep is not None:
+            if prep.dtype != torch.uint8 or prep.device != x.device or prep.numel() < int(
+                    lib().qvx_qmm_prepared_bytes(N, K)):
+                raise ValueError("prep must be qmm_prepare's buffer for this weight, on x's device")
+            check(lib().qvx_qmm_prepared(_ptr(x2), _ptr(w), _ptr(prep), _ptr(out), M, N, K, group_size, bits,
+                                         _ptr(workspace), workspace.numel() * workspace.element_size(), s),
+                  "qvx_qmm_prepared")
+        else:
+            check(lib().qvx_qmm(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size,
+                                bits, _ptr(workspace), workspace.numel() * workspace.element_size(), s),
+                  "qvx_qmm")
     return out
 
 

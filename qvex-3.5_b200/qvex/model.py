@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import torch
 
-from .core import dequantize_rows, quantized_matmul
+from .core import QMV_MAX_M, dequantize_rows, qmm_prepare, quantized_matmul
 
 
 class QLinear:
@@ -18,6 +18,7 @@ class QLinear:
     def __init__(self, w, scales, biases, group_size=64, bits=4):
         self.w, self.scales, self.biases = w, scales, biases
         self.group_size, self.bits = group_size, bits
+        self._prep = None  # the tensor-core path's weight prepass, made on first use
 
     @property
     def out_features(self) -> int:
@@ -27,9 +28,21 @@ class QLinear:
     def in_features(self) -> int:
         return self.w.shape[1] * 32 // self.bits
 
+    def prepared(self):
+        """The weight prepass of the tensor-core path (qmm_prepare), made on the first call
+        with more than QMV_MAX_M rows outside a CUDA-graph capture and kept (the weight is
+        constant); None before that."""
+        if self._prep is None and not torch.cuda.is_current_stream_capturing():
+            self._prep = qmm_prepare(self.scales, self.biases, self.group_size, self.bits)
+        return self._prep
+
     def __call__(self, x, *, out=None, workspace=None):
+        prep = None
+        if x.numel() > QMV_MAX_M * self.in_features:
+            prep = self.prepared()
         return quantized_matmul(x, self.w, self.scales, self.biases, transpose=True,
-                                group_size=self.group_size, bits=self.bits, out=out, workspace=workspace)
+                                group_size=self.group_size, bits=self.bits, out=out, workspace=workspace,
+                                prep=prep)
 
     @staticmethod
     def fuse(layers: list["QLinear"]) -> "QLinear":

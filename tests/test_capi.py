@@ -76,6 +76,20 @@ def test_qmm_workspace_checks(L):
     assert L.qvx_qmm(DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 64, 128, 256, 64, 4, DUMMY, 1024, None) == 6
 
 
+def test_qmm_prepare_checks(L):
+    """The weight prepass buffer: its size (per-row exponents, then per-group multipliers at
+    a 256-byte boundary), and the argument checks of qvx_qmm_prepare / qvx_qmm_prepared."""
+    need = L.qvx_qmm_prepared_bytes(300, 4096)
+    assert need >= 300 * 4 + 300 * 64 * 8
+    assert L.qvx_qmm_prepared_bytes(0, 4096) == 0 and L.qvx_qmm_prepared_bytes(8, 100) == 0
+    assert L.qvx_qmm_prepare(DUMMY, DUMMY, 300, 4096, 64, 4, None, need, None) == 1       # null prep
+    assert L.qvx_qmm_prepare(DUMMY, DUMMY, 300, 4096, 32, 4, DUMMY, need, None) == 2      # group size
+    assert L.qvx_qmm_prepare(DUMMY, DUMMY, 300, 4096, 64, 4, P(4096 + 16), need, None) == 3  # alignment
+    assert L.qvx_qmm_prepare(DUMMY, DUMMY, 300, 4096, 64, 4, DUMMY, need - 1, None) == 6  # too small
+    assert L.qvx_qmm_prepared(DUMMY, DUMMY, DUMMY, DUMMY, 64, 300, 4096, 64, 4, None, 0, None) == 6
+    assert L.qvx_qmm_prepared(DUMMY, DUMMY, P(4096 + 16), DUMMY, 64, 300, 4096, 64, 4, DUMMY, 1 << 30, None) == 3
+
+
 def test_gated_delta_rejects_bad_shapes(L):
     args = [DUMMY] * 11
     assert L.qvx_gated_delta(*args, 1, 1, 3, 32, 128, 128, None) == 1    # Hv % Hk

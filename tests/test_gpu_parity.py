@@ -455,6 +455,23 @@ def test_qmm_and_qmv_agree(qvex):
     assert rel_l2(y_qmm, y_qmv) <= MATMUL_TOL
 
 
+@pytest.mark.parametrize("M,N,K", [(64, 1024, 4096), (16, 300, 192), (200, 4096, 1024), (33, 520, 2048),
+                                   (64, 12352, 4096)])
+def test_qmm_prepared_equals_qmm(qvex, M, N, K):
+    """qvx_qmm_prepared with a prepass made once by qvx_qmm_prepare gives qvx_qmm's bits,
+    twice in a row with the same buffer; QLinear takes that path above QMV_MAX_M rows."""
+    x, _, w, s, b = qmv_inputs(M, K, N, seed=17 * M + N + K)
+    xd, wd, sd, bd = dev(x), dev(w), dev(s), dev(b)
+    ref = host_u16(qvex.quantized_matmul(xd, wd, sd, bd))
+    prep = qvex.core.qmm_prepare(sd, bd)
+    for _ in range(2):
+        got = host_u16(qvex.quantized_matmul(xd, wd, sd, bd, prep=prep))
+        assert np.array_equal(got, ref)
+    lin = qvex.QLinear(wd, sd, bd)
+    assert np.array_equal(host_u16(lin(xd)), ref)
+    assert lin.prepared() is not None
+
+
 def test_qmm_workspace_reuse_and_out(qvex):
     x, _, w, s, b = qmv_inputs(64, 1024, 512, seed=4)
     ref = O.qmm_exact(x, w, s, b)
