@@ -368,9 +368,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      // The waits for stage it + 1 sit between the MMAs of stage it and its commit: the
-      // tensor cores are still working through the queued MMAs while this thread polls,
-      // instead of idling for the ~300 cycles two barrier waits take.
+      // Each stage's MMAs are committed as soon as they are issued: the commit frees the
+      // ring slot and the A stage when the MMAs complete, and the dequant group waiting for
+      // that A stage starts step it + 2 then.  (Committing only after the wait for step
+      // it + 1 made every dequant wait for the other group's, one stage at a time: ~1770
+      // SM cycles per stage at M = 64 and M = 2048 alike, against ~1640 now.)  The thread
+      // then polls for the next stage while the tensor cores work through the queued MMAs.
       auto wait_stage = [&](int i) {
         return mbar_wait(&full[i % NFULL], (uint32_t)(i / NFULL) & 1u, abort_flag, status) &&
                mbar_wait(&full_a[i % DQ_GROUPS], (uint32_t)(i / DQ_GROUPS) & 1u, abort_flag, status);
@@ -390,8 +393,8 @@ __global__ void __launch_bounds__(THREADS, 1)
               tc_mma_ts_f16(tmem + (uint32_t)(h * 128), tmem + A_COL0 + (uint32_t)(a * 2 + h) * 64 + j * 8,
                             smem_desc_sw128(b_addr + (j >> 2) * X_HALF_BYTES + (j & 3) * 32), IDESC,
                             (ks > ks0 || j > 0) ? 1u : 0u);
-          if (ks + 1 < ks1) ok = wait_stage(it + 1);
           tc_commit(&empty[s]);
+          if (ks + 1 < ks1) ok = wait_stage(it + 1);
           if (!ok) break;
         }
         if (ok) tc_commit(acc_full);
