@@ -34,7 +34,12 @@
 //          are not 16-byte multiples).  The accumulator goes back to the MMA issuer as soon
 //          as its last chunk is in registers.
 //   20     TMA producer (one thread).
-//   21     MMA issuer (one thread): 2 x 8 tcgen05.mma per step, one commit per step.
+//   21, 22 MMA issuers (one thread each): accumulator h = warp - 21, 8 tcgen05.mma per step
+//          and one commit per step.  Per-CTA clock stamps showed one thread issuing all
+//          16 MMAs of a step as the limit of the main loop (about 100 SM cycles per MMA,
+//          ~1640 cycles per step at 64 and at 128 tokens alike); the two accumulators take
+//          independent MMAs, so two threads issue them side by side.  Ring slots, A stages
+//          and accumulators are released when both issuers' commits have arrived.
 //
 // Dequantisation with one HFMA2 per two weights.  A nibble masked in place is already an
 // fp16 subnormal: (w & 0x000F000F) is the half2 (q0, q4) * 2^-24 and (w & 0x00F000F0) is
@@ -62,9 +67,10 @@ constexpr int DQ_WARPS_PER_GROUP = 8;  // 2 halves x 4 lane quarters
 constexpr int NUM_DQ_WARPS = DQ_GROUPS * DQ_WARPS_PER_GROUP;
 constexpr int EPI_WARP0 = 16;
 constexpr int WARP_TMA = 20;
-constexpr int WARP_MMA = 21;
-constexpr int THREADS = 22 * 32;
-static_assert(WARP_MMA == WARP_TMA + 1 && THREADS == (WARP_MMA + 1) * 32, "the MMA warp is the last warp");
+constexpr int WARP_MMA = 21;       // MMA issuers: warps 21 and 22, one per accumulator
+constexpr int NUM_MMA_WARPS = 2;
+constexpr int THREADS = (WARP_MMA + NUM_MMA_WARPS) * 32;
+static_assert(WARP_MMA == WARP_TMA + 1, "the MMA warps are the last warps");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t A_COL0 = 256;                    // A stage a, half h: columns A_COL0 + (2a + h) * 64
 constexpr uint32_t CODE_BYTES = BM * (BK / 8) * 4;  // 16 KB: [256 rows][16 words], 64-byte swizzle
@@ -190,11 +196,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NFULL; ++i) mbar_init(&full[i], 1);
-    for (int i = 0; i < S; ++i) mbar_init(&empty[i], 1);
+    for (int i = 0; i < S; ++i) mbar_init(&empty[i], NUM_MMA_WARPS);
     for (int i = 0; i < DQ_GROUPS; ++i) mbar_init(&full_a[i], DQ_WARPS_PER_GROUP);
-    mbar_init(acc_full, 1);
+    mbar_init(acc_full, NUM_MMA_WARPS);
     mbar_init(acc_empty, 4);
-    mbar_init(drain, 1);
+    mbar_init(drain, NUM_MMA_WARPS);
     mbar_init(epi_full, 4);
     mbar_init(epi_free, 1);
     *abort_flag = 0;
@@ -364,8 +370,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_wait_drain(&full[j % NFULL], (uint32_t)(j / NFULL) & 1u, status);
     }
   } else {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
+      const int h = warp - WARP_MMA;  // this thread's accumulator (weight rows 128 h ..)
       int it = 0;
       bool ok = true;
       // Each stage's MMAs are committed as soon as they are issued: the commit frees the
@@ -387,12 +394,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           const uint32_t b_addr = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int j = 0; j < BK / 16; ++j)
-              tc_mma_ts_f16(tmem + (uint32_t)(h * 128), tmem + A_COL0 + (uint32_t)(a * 2 + h) * 64 + j * 8,
-                            smem_desc_sw128(b_addr + (j >> 2) * X_HALF_BYTES + (j & 3) * 32), IDESC,
-                            (ks > ks0 || j > 0) ? 1u : 0u);
+          for (int j = 0; j < BK / 16; ++j)
+            tc_mma_ts_f16(tmem + (uint32_t)(h * 128), tmem + A_COL0 + (uint32_t)(a * 2 + h) * 64 + j * 8,
+                          smem_desc_sw128(b_addr + (j >> 2) * X_HALF_BYTES + (j & 3) * 32), IDESC,
+                          (ks > ks0 || j > 0) ? 1u : 0u);
           tc_commit(&empty[s]);
           if (ks + 1 < ks1) ok = wait_stage(it + 1);
           if (!ok) break;
