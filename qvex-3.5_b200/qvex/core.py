@@ -18,6 +18,11 @@ from ._lib import _P, check, lib
 SUPPORTED_BITS = (4,)
 SUPPORTED_GROUP_SIZES = (64,)
 QMV_MAX_M = 8
+# With a prepared weight (qmm_prepare) the tensor-core path takes M >= QMM_MIN_M_PREPARED:
+# qmv runs token pairs as separate CTA groups that each stream the whole weight, so from 5
+# rows on the tensor-core kernel, which streams it once, is faster (M = 8 over the 9B
+# decode shapes: 1329 against 980 GB/s; M = 4: 1375 against 1746).
+QMM_MIN_M_PREPARED = 5
 
 
 def _stream(t: torch.Tensor) -> _P:
@@ -83,7 +88,8 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     M = prod(x.shape[:-1]) <= 8 runs the SIMT decode kernel, larger M the tcgen05
     tensor-core kernel (which needs a workspace; one is taken from the caching
     allocator when none is given).  ``prep`` (from qmm_prepare of these scales and
-    biases) spares the tensor-core path its per-call weight prepass; same results.
+    biases) spares the tensor-core path its per-call weight prepass (same results) and
+    sends M >= QMM_MIN_M_PREPARED to it as well.
     """
     _check_qparams(group_size, bits)
     if not transpose:
@@ -113,7 +119,7 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     scales = scales.contiguous()
     biases = biases.contiguous()
     s = _stream(x2)
-    if M <= QMV_MAX_M:
+    if M <= QMV_MAX_M and (prep is None or M < QMM_MIN_M_PREPARED):
         check(lib().qvx_qmv(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), M, N, K, group_size,
                             bits, s), "qvx_qmv")
     else:

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import torch
 
-from .core import QMV_MAX_M, dequantize_rows, qmm_prepare, quantized_matmul
+from .core import QMM_MIN_M_PREPARED, dequantize_rows, qmm_prepare, quantized_matmul
 
 
 class QLinear:
@@ -30,15 +30,16 @@ class QLinear:
 
     def prepared(self):
         """The weight prepass of the tensor-core path (qmm_prepare), made on the first call
-        with more than QMV_MAX_M rows outside a CUDA-graph capture and kept (the weight is
-        constant); None before that."""
+        with QMM_MIN_M_PREPARED rows or more outside a CUDA-graph capture and kept (the
+        weight is constant); None before that.  With it, calls of that many rows or more
+        take the tensor-core path."""
         if self._prep is None and not torch.cuda.is_current_stream_capturing():
             self._prep = qmm_prepare(self.scales, self.biases, self.group_size, self.bits)
         return self._prep
 
     def __call__(self, x, *, out=None, workspace=None):
         prep = None
-        if x.numel() > QMV_MAX_M * self.in_features:
+        if x.numel() >= QMM_MIN_M_PREPARED * self.in_features:
             prep = self.prepared()
         return quantized_matmul(x, self.w, self.scales, self.biases, transpose=True,
                                 group_size=self.group_size, bits=self.bits, out=out, workspace=workspace,

@@ -33,7 +33,7 @@ from pathlib import Path
 import torch
 
 from . import glue
-from .core import dequantize_rows, qmv_fused
+from .core import QMM_MIN_M_PREPARED, dequantize_rows, qmv_fused
 from .kernels import gated_delta
 from .model import QEmbedding, QLinear, RecurrentCache
 
@@ -305,8 +305,8 @@ class MLP:
         """silu(x @ gate^T) * (x @ up^T): x [..., H] -> [..., I]."""
         x2 = x.reshape(-1, x.shape[-1])
         gu = self.gate_up
-        if x2.shape[0] <= 8 and gu.in_features % 512 == 0 and gu.in_features <= 12288 and gu.group_size == 64 \
-                and gu.bits == 4:
+        if x2.shape[0] < QMM_MIN_M_PREPARED and gu.in_features % 512 == 0 and gu.in_features <= 12288 \
+                and gu.group_size == 64 and gu.bits == 4:
             y = qmv_fused(x2, gu.w, gu.scales, gu.biases, epilogue="swiglu_pairs", group_size=gu.group_size,
                           bits=gu.bits)
         else:
@@ -453,12 +453,15 @@ class Qwen35:
         """One decode step of B sequences, ids [B, 1] int32 at the device position ``pos``
         (int32 [1]): every state updated in its own buffer and nothing read on the host, so the
         step can be captured once and replayed for every token.  Returns logits [B, 1, V].
-        The fused form (the default where ``fusable``) carries the norms and residual adds in
-        the projection kernels' prologues and epilogues: 5 launches per layer instead of 7, the
-        same bits; ``fused=False`` runs the separate glue kernels."""
+        The fused form (the default where ``fusable`` and B < QMM_MIN_M_PREPARED) carries the
+        norms and residual adds in the projection kernels' prologues and epilogues: 5 launches
+        per layer instead of 7, the same bits; ``fused=False`` runs the separate glue kernels.
+        From QMM_MIN_M_PREPARED sequences on, the default is the separate-glue form, whose
+        projections then run on the tensor-core kernel (faster there than the decode kernel
+        that the fused form is built on)."""
         B = ids.shape[0]
         if fused is None:
-            fused = self.fusable(B)
+            fused = B < QMM_MIN_M_PREPARED and self.fusable(B)
         if fused and not self.fusable(B):
             raise ValueError("the fused decode form needs B <= 8 and projections with K % 512 == 0")
         if not fused:
