@@ -60,6 +60,7 @@ static QmmWorkspace qmm_ws_layout(int M, int N, int K, bool prepared = false) {
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const __nv_bfloat16* __restrict__ x, __half* __restrict__ x16,
                                                       int32_t* __restrict__ xexp, int K) {
   __shared__ float red[8];
+  pdl_grid_sync();  // launched early under programmatic dependent launch; x comes from upstream
   const int m = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)m * K);
   const int n16 = K / 8;  // 16-byte chunks (K % 64 == 0)
@@ -138,7 +139,9 @@ static int qmm_run(const void* x, const uint32_t* w, const void* scales, const v
   int32_t* xexp = reinterpret_cast<int32_t*>(ws + l.off_exp);
   int32_t* fexp = prepared ? const_cast<int32_t*>(prep_fexp) : reinterpret_cast<int32_t*>(ws + l.off_fexp);
   uint2* prm = prepared ? const_cast<uint2*>(prep_prm) : reinterpret_cast<uint2*>(ws + l.off_prm);
-  x_to_f16_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), x16, xexp, K);
+  // under programmatic dependent launch (the main kernel after it is launched normally)
+  launch_pdl(x_to_f16_kernel, dim3((unsigned)M), dim3(256), 0, stream, static_cast<const __nv_bfloat16*>(x), x16, xexp,
+             K);
   int rc = check_launch("qvx_qmm prepass");
   if (rc) return rc;
   if (!prepared) {
