@@ -512,6 +512,7 @@ int qmm_w_prep(const void* scales, const void* biases, int32_t* fexp, uint2* prm
 __global__ void __launch_bounds__(256) qmm_tail_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ y,
                                                            int M, int N, int F, int P, int ntail, int bn) {
   using tc::BM;
+  pdl_grid_sync();  // launched under programmatic dependent launch: the parts come from upstream
   const int tiles_m = (M + bn - 1) / bn, tile = BM * bn;
   const long long total = (long long)ntail * tile;
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -622,7 +623,7 @@ int qmm_tc_launch(const __half* x16, const int32_t* xexp, const int32_t* fexp, c
   const long long total = (long long)ntail * BM * bn;
   long long blocks = (total + 255) / 256;
   if (blocks > (long long)num_sms() * 8) blocks = (long long)num_sms() * 8;
-  qmm_tail_sum_kernel<<<(unsigned)blocks, 256, 0, stream>>>(part, y, M, N, F, P, ntail, bn);
+  launch_pdl(qmm_tail_sum_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, part, y, M, N, F, P, ntail, bn);
   return check_launch("qvx_qmm K-part sum");
 }
 
