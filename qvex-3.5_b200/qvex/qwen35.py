@@ -192,7 +192,7 @@ class Attention:
         G = self.n_heads // self.n_kv
         ws, ns = None, 0
         if G * L <= 8:
-            ns = glue.default_splits(B, self.n_kv, x.device)
+            ns = glue.default_splits(B, self.n_kv, x.device, cap=cache.k.shape[2])
             ws = self.workspace(B, L, ns)
         o = glue.attention(qkv, self.q_norm, self.k_norm, self.cfg.rms_norm_eps, self.inv_freq, cache.k, cache.v,
                            cache.offset if pos is None else pos, self.n_heads, self.n_kv, self.head_dim,

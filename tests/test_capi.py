@@ -194,3 +194,16 @@ def test_qk_condition_rejects(L):
     assert L.qvx_qk_condition(DUMMY, DUMMY, DUMMY, DUMMY, -1, 128, None) == 1
     assert L.qvx_qk_condition(P(4098), DUMMY, DUMMY, DUMMY, 8, 128, None) == 3
     assert L.qvx_qk_condition(None, None, None, None, 0, 128, None) == 0       # nothing to do
+
+
+def test_attention_split_count_host_logic():
+    """Decode attention's key ranges per KV head: one CTA per SM over all (sequence, KV
+    head) pairs, at most 64, and no more than one range per 128 cache positions."""
+    from qvex.glue import split_count
+    assert split_count(1, 8, 148) == 18
+    assert split_count(1, 8, 148, cap=4352) == 18
+    assert split_count(1, 8, 148, cap=1280) == 10
+    assert split_count(1, 8, 148, cap=100) == 1
+    assert split_count(64, 8, 148, cap=4096) == 1
+    assert split_count(1, 1, 148) == 64
+    assert split_count(4, 2, 148, cap=300) == 3
