@@ -25,7 +25,7 @@
 // stages; step L writes stage L % 2, which is free once the MMAs of step L - 2 are done,
 // i.e. once empty[(L - 2) % S] has completed that step's phase: no separate barrier.
 //
-// Warp roles (22 warps):
+// Warp roles (23 warps):
 //   0..15  dequant: two groups of 8 warps take alternate steps (group g owns A stage g);
 //          within a group warp w owns TMEM lanes 32*(w%4).. of weight-row half (w/4)%2,
 //          one weight row per thread, and writes its 128 fp16 values (64 columns).
